@@ -1,0 +1,178 @@
+/*
+ * strata_cuda.h -- C ABI of the B200 quantized-expert library (libstrata_cuda.so).
+ *
+ * The library multiplies straight from GGUF quantized blocks: the expert matvecs, the SwiGLU down product,
+ * the prefill tile product on tcgen05 tensor cores, and the MoE router, top-k and combine. Every entry point
+ * takes plain device pointers, sizes and a cudaStream_t passed as void*; it enqueues work on that stream and
+ * returns without waiting. It never allocates: outputs and workspaces belong to the caller. Return value 0 is
+ * success, a negative SC_ERR_* code a rejected call (nothing was enqueued) or a CUDA launch error.
+ *
+ * Kernels that find a bad expert id, or give up a bounded wait, record an SC_ERR_* code in the caller's
+ * device int `err` (when not NULL) with atomicCAS(err, 0, code) and skip the work; they never trap.
+ *
+ * Each declaration names the interface of strata-mlx (cantrellsolutions/strata-mlx, paths inside that
+ * project) that it replaces. Tensors are row-major; a stack of experts is (experts, rows, cols) weights held
+ * as rows of GGUF blocks, row after row, exactly the bytes of the file (strata_mlx/gguf.py:105-115).
+ */
+#ifndef STRATA_CUDA_H
+#define STRATA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SC_API __attribute__((visibility("default")))
+#else
+#define SC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_ABI_VERSION 1
+
+/* block types: strata_mlx/blocks.py:35-38 (BLOCK), plus Q8_0 (strata_mlx/gguf.py:27) for dense tensors */
+enum {
+  SC_Q2_0 = 0, SC_IQ4_NL = 1, SC_IQ4_XS = 2, SC_IQ3_S = 3, SC_IQ3_XXS = 4,
+  SC_IQ2_S = 5, SC_IQ2_XS = 6, SC_IQ2_XXS = 7, SC_IQ1_M = 8, SC_Q3_K = 9, SC_Q8_0 = 10,
+  SC_NUM_KINDS = 11
+};
+
+/* activation / output types */
+enum { SC_F32 = 0, SC_F16 = 1, SC_BF16 = 2 };
+
+/* index types accepted by sc_tiles_of */
+enum { SC_I32 = 0, SC_U32 = 1, SC_I64 = 2 };
+
+/* error codes */
+enum {
+  SC_OK = 0,
+  SC_ERR_KIND = -1,        /* unknown block type                                          */
+  SC_ERR_SHAPE = -2,       /* a row does not end on a block, or a size out of range          */
+  SC_ERR_DTYPE = -3,       /* activation type not taken by this entry point                  */
+  SC_ERR_ALIGN = -4,       /* a pointer is not aligned as the entry point needs              */
+  SC_ERR_ARG = -5,         /* a NULL or negative argument                                    */
+  SC_ERR_CUDA = -6,        /* the launch failed (cudaGetLastError)                           */
+  SC_ERR_WORKSPACE = -7,   /* workspace too small                                            */
+  SC_ERR_UNSUPPORTED = -8, /* a combination this build does not take (caller falls back)     */
+  SC_ERR_TIMEOUT = -9,     /* recorded by a kernel: a bounded wait gave up                    */
+  SC_ERR_INDEX = -10       /* recorded by a kernel: an expert id >= the number of experts    */
+};
+
+/* library version (SC_ABI_VERSION) */
+SC_API int sc_version(void);
+
+/* a static description of an error code */
+SC_API const char* sc_error_string(int code);
+
+/* strata_mlx/blocks.py:35-38 BLOCK[kind]: weights per block and bytes per block */
+SC_API int sc_block_info(int kind, int* per_block, int* block_bytes);
+
+/* strata_mlx/blocks.py:397-404 dequantize(blocks, kind, shape, dtype): every weight of `mats` matrices of
+ * rows x cols as out_dtype, out (mats, rows, cols). The float32 values are those of the reference's unpack32
+ * (blocks.py:57-193) bit for bit; float16/bfloat16 outputs are those rounded to nearest even. */
+SC_API int sc_dequant(int kind, const void* blocks, int64_t mats, int rows, int cols, int out_dtype, void* out,
+               void* stream);
+
+/* strata_mlx/blocks.py:420-436 BlockSwitchLinear.__call__ (the _MATVEC kernel, blocks.py:196-220):
+ * out[p, r] = W[idx[p], r, :] . x[p / share, :] for p < pairs, sums in float32, out (pairs, rows) in the type of x.
+ * blocks: (experts, rows, cols) stack. Pairs that name the same expert read its blocks once. */
+SC_API int sc_expert_matvec(int kind, const void* blocks, int experts, int rows, int cols, const uint32_t* idx, int pairs,
+                     int share, const void* x, int dtype, void* out, int* err, void* stream);
+
+/* strata_mlx/blocks.py:331-346 matvec_separate(experts, kind, rows, cols, x, share): as sc_expert_matvec, pair p's
+ * expert being its own buffer bases[p] (a device array of `pairs` device pointers, each rows x cols of blocks). */
+SC_API int sc_expert_matvec_ptrs(int kind, const void* const* bases, int pairs, int rows, int cols, int share, const void* x,
+                          int dtype, void* out, int* err, void* stream);
+
+/* strata_mlx/blocks.py:383-394 window_matvec(blocks, kind, rows, cols, x): out[t] = W . x[t], one layer, tokens rows of x */
+SC_API int sc_window_matvec(int kind, const void* blocks, int rows, int cols, const void* x, int dtype, int tokens, void* out,
+                     int* err, void* stream);
+
+/* strata_mlx/blocks.py:782-798 matvec_glu(lin, idx, gate, up) (the _MATVEC_GLU kernel, blocks.py:225-259):
+ * out[p] = W[idx[p]] . h[p] with h = swiglu(gate[p], up[p]) worked out in shared memory.
+ * glu 0: mlx-lm's rounding (sigmoid in float32 rounded to the type, then two products in the type), as _MATVEC_GLU;
+ * glu 1: silu(g) * u in float32 rounded once, as the Q2_0 down table's (blocks.py:706-715, lookup_down_glu :740-760). */
+SC_API int sc_matvec_glu(int kind, const void* blocks, int experts, int rows, int cols, const uint32_t* idx, int pairs,
+                  const void* gate, const void* up, int dtype, int glu, void* out, int* err, void* stream);
+
+/* strata_mlx/blocks.py:808-818 (switch_glu's per-pair branch: gate(x), up(x), swiglu) in one kernel:
+ * h[p, r] = swiglu(W_gate[idx[p], r] . x[p / share], W_up[idx[p], r] . x[p / share]), mlx-lm's rounding.
+ * gate and up are stacks of the same kind and shape (experts, rows, cols). */
+SC_API int sc_expert_gate_up(int kind, const void* gate, const void* up, int experts, int rows, int cols, const uint32_t* idx,
+                      int pairs, int share, const void* x, int dtype, void* h, int* err, void* stream);
+
+/* mlx-lm swiglu as strata_mlx/blocks.py:230-238 restates it, elementwise over n values of dtype */
+SC_API int sc_swiglu(const void* gate, const void* up, int64_t n, int dtype, void* out, void* stream);
+
+/* strata_mlx/fused.py:357-390 WindowLinear.__call__: logits (tokens, rows) float32 = x . W^T,
+ * W (rows, cols) float16, x (tokens, cols) of dtype, float32 sums. */
+SC_API int sc_router(const void* w, int rows, int cols, const void* x, int dtype, int tokens, float* logits, void* stream);
+
+/* strata_mlx/fused.py:424-436 top_k(logits, k): the k largest of each of `rows` rows of n float32 logits, largest
+ * first, ties to the lower index (the order of the reference's _TOPK kernel, fused.py:400-418). idx (rows, k). */
+SC_API int sc_top_k(const float* logits, int rows, int n, int k, uint32_t* idx, void* stream);
+
+/* strata_mlx/fused.py:490-491: top_k as above, then weights (rows, k) float32 = softmax over the chosen logits */
+SC_API int sc_top_k_softmax(const float* logits, int rows, int n, int k, uint32_t* idx, float* weights, void* stream);
+
+/* strata_mlx/fused.py:467-481 moe_combine(y, w, g, s): out[t] = T(sum_k y[t,k] w[t,k]) + T(T(sigmoid(g[t])) s[t]),
+ * the k terms added in MLX's col_reduce order (fused.py:448-462). y (rows, k, d), w (rows, k) float32,
+ * g (rows), s (rows, d), out (rows, d); y, g, s, out of dtype. */
+SC_API int sc_moe_combine(const void* y, const float* w, const void* g, const void* s, int rows, int k, int d, int dtype,
+                   void* out, void* stream);
+
+/* strata_mlx/blocks.py:539-563 tiles_of(indices, experts): the pairs of idx (pairs = tokens * k entries, of
+ * idx_dtype) laid out in tiles of 16 slots, each tile one expert's, in a number of tiles that depends only on
+ * the number of pairs: max_tiles = pairs / 16 + min(experts, pairs).
+ * tile_expert (max_tiles): a tile's expert, or `experts` for a tile nothing fills; token (max_tiles * 16): the
+ * token (pair / k) of each slot, 0 for empty slots; where (pairs): each pair's slot.
+ * workspace: sc_tiles_of_workspace(experts) bytes of device memory. */
+SC_API int sc_tiles_of(const void* idx, int idx_dtype, int pairs, int k, int experts, uint32_t* tile_expert, uint32_t* token,
+                uint32_t* where, void* workspace, size_t workspace_bytes, void* stream);
+SC_API size_t sc_tiles_of_workspace(int experts);
+
+/* strata_mlx/blocks.py:516-536 tile_matmul(blocks, kind, shape, a, tile_expert): c (P, rows) float32 =
+ * W[tile_expert[p / 16]] . a[p] for a (P, cols) of a_dtype, P a multiple of 16; the weights are rounded to
+ * a_dtype before they multiply; float32 sums. Tiles naming no expert (>= experts) are left unwritten.
+ * bfloat16 / float16 `a` run on the tcgen05 tensor cores; float32 `a` on the CUDA cores. */
+SC_API int sc_tile_matmul(int kind, const void* blocks, int experts, int rows, int cols, const void* a, int a_dtype, int P,
+                   const uint32_t* tile_expert, float* c, void* stream);
+
+/* One MoE block in decode, strata_mlx/fused.py:487-497 (_Routed.__call__): the router (fused.py:377-390), top_k
+ * (:424-436), the softmax over the chosen logits (:491), the routed SwiGLU experts (blocks.py:801-829), the
+ * shared expert and its gate, and moe_combine (fused.py:467-481), for a window of 1..8 tokens. */
+typedef struct sc_moe_layer {
+  int hidden;              /* H: x and out are (tokens, H)                                       */
+  int inter;               /* I: inner size of a routed expert                                   */
+  int experts;             /* E                                                                  */
+  int top_k;               /* K <= 16                                                            */
+  int kind_gate, kind_up, kind_down;
+  const void* gate;        /* (E, I, H) blocks                                                    */
+  const void* up;          /* (E, I, H) blocks                                                    */
+  const void* down;        /* (E, H, I) blocks                                                    */
+  const void* router;      /* (E, H) float16                                                      */
+  int shared_inter;        /* inner size of the shared expert, 0 for none                         */
+  int kind_sgate, kind_sup, kind_sdown;
+  const void* sgate;       /* (shared_inter, H) blocks                                            */
+  const void* sup;         /* (shared_inter, H) blocks                                            */
+  const void* sdown;       /* (H, shared_inter) blocks                                            */
+  const void* shared_gate; /* (H) float16: the shared expert's gate, a product with x               */
+  int dtype;               /* activations: SC_F16 or SC_BF16                                      */
+} sc_moe_layer;
+
+/* out (tokens, H) of layer->dtype. workspace: sc_moe_decode_workspace(layer, tokens) bytes of device memory,
+ * whose first int is the kernels' error word. Results a caller may read back from the workspace:
+ * sc_moe_decode_routes(). */
+SC_API int sc_moe_decode_layer(const sc_moe_layer* layer, const void* x, int tokens, void* out, void* workspace,
+                        size_t workspace_bytes, void* stream);
+SC_API size_t sc_moe_decode_workspace(const sc_moe_layer* layer, int tokens);
+/* Offsets in the workspace of the last call's routes: idx (tokens, K) uint32 and weights (tokens, K) float32. */
+SC_API int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_t* idx_offset, size_t* weight_offset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STRATA_CUDA_H */

@@ -1,0 +1,31 @@
+// Version, error strings and block-type sizes of the C ABI.
+#include "common.cuh"
+
+using namespace sc;
+
+extern "C" int sc_version(void) { return SC_ABI_VERSION; }
+
+extern "C" const char* sc_error_string(int code) {
+  switch (code) {
+    case SC_OK: return "ok";
+    case SC_ERR_KIND: return "unknown block type";
+    case SC_ERR_SHAPE: return "a row does not end on a block, or a size is out of range";
+    case SC_ERR_DTYPE: return "activation type not taken by this entry point";
+    case SC_ERR_ALIGN: return "a pointer or size is not aligned as the entry point needs";
+    case SC_ERR_ARG: return "a NULL or negative argument";
+    case SC_ERR_CUDA: return "a CUDA launch failed";
+    case SC_ERR_WORKSPACE: return "the workspace is too small";
+    case SC_ERR_UNSUPPORTED: return "a combination this build does not take";
+    case SC_ERR_TIMEOUT: return "a kernel gave up a bounded wait";
+    case SC_ERR_INDEX: return "an expert id is not below the number of experts";
+    default: return "unknown error code";
+  }
+}
+
+extern "C" int sc_block_info(int kind, int* per_block, int* block_bytes) {
+  const BlockInfo b = block_info(kind);
+  if (b.per_block == 0) return SC_ERR_KIND;
+  if (per_block) *per_block = b.per_block;
+  if (block_bytes) *block_bytes = b.block_bytes;
+  return SC_OK;
+}

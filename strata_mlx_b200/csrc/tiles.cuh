@@ -1,0 +1,21 @@
+// Prefill tile geometry (strata_mlx/blocks.py:462-463, :511-513) and the tensor-core tile product's launcher.
+#pragma once
+
+#include "common.cuh"
+
+namespace sc {
+
+constexpr int TOKENS_TILE = 16;  // slots of a tile (blocks.py:463 TOKENS_TILE)
+
+// blocks.py:511-513 tileable: rows by 64, columns by 64, and rows that end on a block
+inline bool tileable(int kind, int rows, int cols) {
+  const BlockInfo b = block_info(kind);
+  return b.per_block && rows > 0 && cols > 0 && rows % 64 == 0 && cols % 64 == 0 && cols % b.per_block == 0;
+}
+
+// The tcgen05 tile product (tile_mma.cu) for float16 / bfloat16 activations; SC_ERR_UNSUPPORTED where it
+// does not take the call (the caller then runs the CUDA-core kernel).
+int tile_mma_launch(int kind, const uint8_t* blocks, int experts, int rows, int cols, int64_t rbytes, const void* a,
+                    int a_dtype, int P, const uint32_t* tile_expert, float* c, cudaStream_t s);
+
+}  // namespace sc

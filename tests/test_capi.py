@@ -1,0 +1,79 @@
+"""The C ABI without a GPU: the library loads, exports every symbol include/strata_cuda.h declares, and turns
+bad arguments into error codes before touching CUDA. No kernel is launched here."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from strata_mlx_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "strata_cuda.h")
+
+
+def declared() -> list:
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^SC_API\s+[\w\s\*]+?\b(sc_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    lib = _lib.load()
+    names = declared()
+    assert len(names) >= 20
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_version_and_error_strings():
+    lib = _lib.load()
+    assert lib.sc_version() == _lib.ABI_VERSION
+    for code in list(_lib.ERRORS) + [0]:
+        s = lib.sc_error_string(code).decode()
+        assert s and s != "unknown error code"
+    assert lib.sc_error_string(12345).decode() == "unknown error code"
+
+
+def test_block_info_is_the_reference_table():
+    from strata_mlx_b200.blocks import BLOCK
+
+    lib = _lib.load()
+    for kind, want in list(BLOCK.items()) + [("Q8_0", (32, 34))]:
+        pb, bb = ctypes.c_int(), ctypes.c_int()
+        assert lib.sc_block_info(_lib.KINDS[kind], ctypes.byref(pb), ctypes.byref(bb)) == 0
+        assert (pb.value, bb.value) == want
+    assert lib.sc_block_info(99, None, None) == -1
+
+
+def test_bad_arguments_are_rejected_before_any_launch():
+    lib = _lib.load()
+    fake = 0x1000  # never dereferenced: every call below fails its checks first
+    assert lib.sc_dequant(99, fake, 1, 2, 256, 0, fake, None) == -1  # unknown kind
+    assert lib.sc_dequant(_lib.KINDS["IQ3_S"], fake, 1, 2, 640, 0, fake, None) == -2  # 640 does not end on a block
+    assert lib.sc_dequant(0, None, 1, 2, 64, 0, fake, None) == -5
+    assert lib.sc_expert_matvec(0, fake, 4, 8, 100, fake, 1, 1, fake, 0, fake, None, None) == -2
+    assert lib.sc_expert_matvec(0, fake, 4, 8, 128, fake, 1, 1, fake, 7, fake, None, None) == -3  # bad dtype
+    assert lib.sc_router(fake, 8, 12, fake, 0, 1, fake, None) == -4  # cols not a multiple of 8
+    assert lib.sc_top_k(fake, 1, 8, 17, fake, None) == -2  # k above 16
+    assert lib.sc_tiles_of(fake, 0, 10, 2, 4, fake, fake, fake, None, 0, None) == -7
+    assert lib.sc_tile_matmul(0, fake, 4, 100, 128, fake, 1, 16, fake, fake, None) == -2  # rows not by 64
+    assert lib.sc_moe_decode_workspace(None, 1) == 0
+
+
+def test_tiles_of_workspace_grows_with_experts():
+    lib = _lib.load()
+    assert lib.sc_tiles_of_workspace(512) > lib.sc_tiles_of_workspace(8) > 0
+
+
+def test_products_refuse_tensors_off_the_gpu():
+    """No CPU fallback: the drop-in raises rather than compute anywhere but on CUDA."""
+    from strata_mlx_b200 import blocks
+
+    b = torch.zeros(18 * 4, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="CUDA"):
+        blocks.BlockSwitchLinear(b, "Q2_0", (1, 4, 64))
+    with pytest.raises(ValueError, match="CUDA"):
+        blocks.dequantize(b, "Q2_0", (4, 64))
