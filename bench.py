@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-expert MoE decode path on B200s.
+
+A step decodes one token (per rank) through a chain of L distinct MoE layers of configuration 2: hidden 2048,
+512 experts of SwiGLU inner 512 as GGUF blocks, top-10 softmax router (float16 weights), a shared expert of
+inner 512 with its sigmoid gate, bfloat16 activations. Experts alternate Q2_0 / IQ3_S layer by layer. Weights
+are seeded synthetic blocks made in HBM (no model files exist); each layer's weights are distinct, so a step
+reads ~0.6 GB of routed expert blocks from HBM, far more than the 126 MB L2, with a fresh token every step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line on rank 0. `value` is tokens/s with the token already in HBM (the chain replayed as a CUDA graph);
+`e2e` is the same through the public API (strata_mlx_b200.fused.DecodeGraph) from pinned host memory, copies in
+the timed region. `roofline` times the dominant kernel (the routed experts' fused gate/up matvec) alone, 48
+launches in a graph, against the measured HBM copy bandwidth. `cpu_baseline` is the C oracle on the host cores.
+`--impl reference` times the C oracle (strata-mlx's block decode and MoE block restated in C: the reference's own
+implementation is Metal, which has no CPU form) on all host cores, for the same config and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, K, IS = 2048, 512, 512, 10, 512
+METRIC = "decode tok/s and expert-matvec HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+BLOCK = {"Q2_0": (64, 18), "IQ3_S": (256, 110), "IQ3_XXS": (256, 98)}
+
+
+def row_bytes(kind: str, cols: int) -> int:
+    pb, bb = BLOCK[kind]
+    return cols // pb * bb
+
+
+def kind_of(layer: int, mode: str) -> str:
+    return ("Q2_0" if layer % 2 == 0 else "IQ3_S") if mode == "mixed" else mode
+
+
+def peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---- distributed plumbing
+
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def reduce_max(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---- clocks during the timed region
+
+
+class Clocks:
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(device_index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---- the workload
+
+
+def build_layers(n_layers: int, mode: str, rank: int, device):
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import fused as F
+    from strata_mlx_b200.synthetic import blocks_cuda
+
+    layers = []
+    for l in range(n_layers):
+        kind = kind_of(l, mode)
+        seed = 1000 * rank + 10 * l
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + 7)
+        lin = {
+            "gate": B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, seed + 1, device), kind, (E, I, H)),
+            "up": B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, seed + 2, device), kind, (E, I, H)),
+            "down": B.BlockSwitchLinear(blocks_cuda(kind, E, H, I, seed + 3, device), kind, (E, H, I)),
+            "sgate": B.BlockSwitchLinear(blocks_cuda(kind, 1, IS, H, seed + 4, device), kind, (1, IS, H)),
+            "sup": B.BlockSwitchLinear(blocks_cuda(kind, 1, IS, H, seed + 5, device), kind, (1, IS, H)),
+            "sdown": B.BlockSwitchLinear(blocks_cuda(kind, 1, H, IS, seed + 6, device), kind, (1, H, IS)),
+        }
+        router = (torch.randn((E, H), generator=g, device=device) * 0.02).half()
+        sgw = (torch.randn((H,), generator=g, device=device) * 0.02).half()
+        layer = F.MoEDecodeLayer(router, lin["gate"], lin["up"], lin["down"], K,
+                                 shared=(lin["sgate"], lin["sup"], lin["sdown"]), shared_gate=sgw, dtype=torch.bfloat16)
+        layer.kind, layer.lin = kind, lin
+        layers.append(layer)
+    return layers
+
+
+def time_gate_up(layers, graph, device, reps: int) -> dict:
+    """The routed experts' fused gate/up kernel alone: one launch per layer with the routes that layer chose for
+    the last token, 48 launches captured in a graph, timed with CUDA events on the graph's stream."""
+    from strata_mlx_b200 import _lib
+    from strata_mlx_b200._lib import KINDS, ptr
+
+    lib = _lib.lib()
+    outs = [torch.empty((K, I), dtype=torch.bfloat16, device=device) for _ in layers]
+    routes = [l.routes(1, device)[0].clone() for l in layers]
+    err = _lib.error_word(device)
+    s = torch.cuda.Stream(device=device)
+
+    def launch_all():
+        for l, o, r in zip(layers, outs, routes):
+            g, u = l.lin["gate"], l.lin["up"]
+            rc = lib.sc_expert_gate_up(KINDS[l.kind], ptr(g.blocks), ptr(u.blocks), E, I, H, ptr(r), K, K, ptr(graph.x),
+                                       2, ptr(o), ptr(err), s.cuda_stream)
+            _lib.check(rc, "gate_up")
+
+    with torch.cuda.stream(s):
+        launch_all()
+    s.synchronize()
+    cg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(cg, stream=s):
+        launch_all()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            cg.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            cg.replay()
+        e1.record(s)
+    s.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * len(layers))
+    bytes_per = sum(2 * K * I * row_bytes(l.kind, H) + H * 2 + K * I * 2 for l in layers) / len(layers)
+    return {"ms_per_launch": ms, "bytes_per_launch": bytes_per}
+
+
+def read_traffic(kinds: list) -> float | None:
+    """Per-launch DRAM bytes (read + write) of the gate/up kernel from the committed ncu summary
+    (profiles/traffic.txt, one line per block type), averaged over the chain's layers; None unless every block
+    type of the chain was captured."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    got = {}
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) == 2 and parts[0].startswith("gate_up_") and parts[0].endswith("_bytes_per_launch"):
+                got[parts[0][len("gate_up_"):-len("_bytes_per_launch")]] = float(parts[1])
+    except OSError:
+        return None
+    if not all(k in got for k in kinds):
+        return None
+    return sum(got[k] for k in kinds) / len(kinds)
+
+
+def cpu_sample(mode: str, seconds: float, all_threads: bool) -> dict:
+    """The C oracle on the host cores: one layer of each block type (the same shapes), timed for about
+    `seconds`, scaled to the 48-layer step."""
+    from oracle import cref
+    from strata_mlx_b200.synthetic import layer_numpy
+
+    threads = cref.threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(12345)
+    kinds = ["Q2_0", "IQ3_S"] if mode == "mixed" else [mode]
+    per_layer = {}
+    for kind in kinds:
+        L = layer_numpy(rng, H, I, E, (kind, kind, kind), shared_inter=IS)
+        layer = cref.Layer(L, H, I, E, K, "bfloat16", shared_inter=IS)
+        x = rng.standard_normal((1, H)).astype(np.float32)
+        layer(x)  # warm
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / len(kinds) or n < 2:
+            layer(rng.standard_normal((1, H)).astype(np.float32))
+            n += 1
+        per_layer[kind] = (time.perf_counter() - t0) / n
+    return {"per_layer_s": per_layer, "threads": threads}
+
+
+def step_seconds(per_layer: dict, n_layers: int, mode: str) -> float:
+    return sum(per_layer[kind_of(l, mode)] for l in range(n_layers))
+
+
+def run_reference(args, world, rank) -> None:
+    """--impl reference: the C oracle (the reference's block decode and MoE block restated in C) on all host
+    cores, rank 0 only; each step a bounded sample of the 48-layer chain."""
+    if rank != 0:
+        return
+    from oracle import cref
+    from strata_mlx_b200.synthetic import layer_numpy
+
+    threads = cref.threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(777)
+    kinds = ["Q2_0", "IQ3_S"] if args.kinds == "mixed" else [args.kinds]
+    host = {k: cref.Layer(layer_numpy(rng, H, I, E, (k, k, k), shared_inter=IS), H, I, E, K, "bfloat16", shared_inter=IS)
+            for k in kinds}
+    # one probe layer of each kind sizes the sample: (steps + warmup) samples within about two minutes
+    probe = {}
+    for k in kinds:
+        host[k](rng.standard_normal((1, H)).astype(np.float32))
+        t0 = time.perf_counter()
+        host[k](rng.standard_normal((1, H)).astype(np.float32))
+        probe[k] = time.perf_counter() - t0
+    full = step_seconds(probe, args.layers, args.kinds)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    sample_layers = max(len(kinds), min(args.layers, int(args.layers * budget / max(full, 1e-9))))
+    sample_layers -= sample_layers % len(kinds)
+
+    def step():
+        t0 = time.perf_counter()
+        for l in range(sample_layers):
+            host[kind_of(l, args.kinds)](rng.standard_normal((1, H)).astype(np.float32))
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        step()
+    total = sum(step() for _ in range(args.steps))
+    ms = total / args.steps * args.layers / sample_layers * 1000.0
+    value = 1000.0 / ms
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": workload_config(args, world),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{sample_layers} of {args.layers} layers per step, one token, scaled to the chain"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, world) -> dict:
+    return {"workload": "config2: one MoE layer decode, batch 1 per rank (hidden 2048, 512 experts x SwiGLU inter 512, "
+                        "top-10 softmax router, shared expert inter 512), experts "
+                        + ("Q2_0 / IQ3_S alternating" if args.kinds == "mixed" else args.kinds)
+                        + f", chained over {args.layers} distinct layers",
+            "layers": args.layers, "tokens_per_rank_per_step": 1, "hidden": H, "experts": E, "inter": I, "top_k": K,
+            "shared_inter": IS, "global_batch": world, "parallelism": "replicas" if world > 1 else "single",
+            "l2": "inputs larger than L2: ~0.6 GB of distinct routed-expert blocks per step, a fresh token each step"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--kinds", default="mixed", choices=["mixed", "Q2_0", "IQ3_S"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    from strata_mlx_b200 import _lib
+    from strata_mlx_b200 import fused as F
+
+    _lib.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    layers = build_layers(args.layers, args.kinds, rank, device)
+    graph = F.DecodeGraph(layers, tokens=1, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99 + rank)
+    n_tok = args.steps + args.warmup
+    xs = torch.randn((n_tok, H), generator=gen, device=device).to(torch.bfloat16)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+
+    # ---- value: the chain replayed from HBM-resident tokens
+    for i in range(args.warmup):
+        graph.x.copy_(xs[i : i + 1])
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.steps):
+        graph.x.copy_(xs[args.warmup + i : args.warmup + i + 1])
+        graph.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = reduce_max(e0.elapsed_time(e1) / args.steps, world)
+    barrier(world)
+    _lib.check_device_errors(device)
+
+    # ---- e2e: the public call, pinned host token in, host result out, every step
+    host_x = xs.cpu().pin_memory()
+    for i in range(args.warmup):
+        graph(host_x[i])
+    barrier(world)
+    e2e_steps = min(args.steps, 500)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        graph(host_x[(args.warmup + i) % n_tok])
+    e2e_ms = reduce_max((time.perf_counter() - t0) / e2e_steps * 1000.0, world)
+
+    # ---- the dominant kernel alone
+    gu = time_gate_up(layers, graph, device, reps=50)
+    pk = peaks()
+    achieved = gu["bytes_per_launch"] / (gu["ms_per_launch"] * 1e-3) / 1e9
+    traffic = read_traffic([l.kind for l in layers])
+
+    line = {"metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: seeded GGUF blocks and float16 router made in HBM",
+            "config": workload_config(args, world),
+            "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
+                    "api": "strata_mlx_b200.fused.DecodeGraph.__call__"},
+            "roofline": {"bound": "hbm", "kernel": "mv_kernel GATEUP (routed experts' fused gate/up matvec)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "peak_source": pk["source"], "traffic": traffic,
+                         "bytes_per_launch": gu["bytes_per_launch"], "us_per_launch": gu["ms_per_launch"] * 1e3},
+            "expert_matvec_gbs": achieved, "expert_matvec_frac_of_8tbs": achieved / 8000.0,
+            "gpu_launches": 8 * args.layers, "clocks": clk}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cb = cpu_sample(args.kinds, 12.0, True)
+        cpu_ms = step_seconds(cb["per_layer_s"], args.layers, args.kinds) * 1000.0
+        line["cpu_baseline"] = {"value": 1000.0 / cpu_ms, "unit": "tok/s", "cores": cb["threads"], "kind": "port",
+                                "sample": "one layer of each block type timed for ~12 s, scaled to the 48-layer step"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

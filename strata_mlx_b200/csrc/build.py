@@ -67,8 +67,11 @@ def _compile(unit: tuple, verbose: bool, extra: list) -> str:
 
 def build(jobs: int = 8, verbose: bool = False, extra: list | None = None) -> str:
     os.makedirs(BUILD, exist_ok=True)
-    sys.path.insert(0, HERE)
-    import gen_tables
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("sc_gen_tables", os.path.join(HERE, "gen_tables.py"))
+    gen_tables = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen_tables)
 
     gen_tables.main(os.path.join(HERE, "iq_tables.h"))
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:

@@ -216,3 +216,49 @@ class MoEDecodeLayer:
         idx = ws[io.value : io.value + tokens * k * 4].view(torch.int32).view(torch.uint32).reshape(tokens, k)
         w = ws[wo.value : wo.value + tokens * k * 4].view(torch.float32).reshape(tokens, k)
         return idx, w
+
+
+class DecodeGraph:
+    """A stack of decode layers (MoEDecodeLayer) replayed as one CUDA graph: the call a serving loop makes per
+    decoded window. __call__ takes the window's activations on the host (pinned, or any CPU tensor), copies them
+    in, runs every layer, and returns the last layer's output on the host. `layers` each take the previous
+    layer's input when `chain` is False (each layer reads the window itself), or the previous output when True."""
+
+    def __init__(self, layers: list, tokens: int, device=None, chain: bool = False):
+        self.layers, self.tokens, self.chain = layers, tokens, chain
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        H, dt = layers[0].hidden, layers[0].dtype
+        self.x = torch.zeros((tokens, H), dtype=dt, device=dev)
+        self.outs = [torch.zeros((tokens, H), dtype=dt, device=dev) for _ in layers]
+        self.host_in = torch.zeros((tokens, H), dtype=dt).pin_memory()
+        self.host_out = torch.zeros((tokens, H), dtype=dt).pin_memory()
+        for l in layers:
+            l.workspace(tokens, dev)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(self.stream):
+            self.run_layers()  # warm: kernel attributes are set outside the capture
+        self.stream.synchronize()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.run_layers()
+
+    def run_layers(self) -> None:
+        x = self.x
+        for l, o in zip(self.layers, self.outs):
+            l(x, out=o)
+            if self.chain:
+                x = o
+
+    def replay(self) -> torch.Tensor:
+        """Runs the graph on the activations already in self.x (device-resident); returns the last output."""
+        self.graph.replay()
+        return self.outs[-1]
+
+    def __call__(self, x_host: torch.Tensor) -> torch.Tensor:
+        s = torch.cuda.current_stream()
+        self.host_in.copy_(x_host.reshape(self.host_in.shape))
+        self.x.copy_(self.host_in, non_blocking=True)
+        self.graph.replay()
+        self.host_out.copy_(self.outs[-1], non_blocking=True)
+        s.synchronize()
+        return self.host_out
