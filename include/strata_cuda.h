@@ -57,7 +57,8 @@ enum {
   SC_ERR_WORKSPACE = -7,   /* workspace too small                                            */
   SC_ERR_UNSUPPORTED = -8, /* a combination this build does not take (caller falls back)     */
   SC_ERR_TIMEOUT = -9,     /* recorded by a kernel: a bounded wait gave up                    */
-  SC_ERR_INDEX = -10       /* recorded by a kernel: an expert id >= the number of experts    */
+  SC_ERR_INDEX = -10,      /* recorded by a kernel: an expert id >= the number of experts    */
+  SC_ERR_SCRATCH = -11     /* the call needs more scratch than SC_NOALLOC_SCRATCH_BYTES       */
 };
 
 /* library version (SC_ABI_VERSION) */
@@ -170,6 +171,24 @@ SC_API int sc_moe_decode_layer(const sc_moe_layer* layer, const void* x, int tok
 SC_API size_t sc_moe_decode_workspace(const sc_moe_layer* layer, int tokens);
 /* Offsets in the workspace of the last call's routes: idx (tokens, K) uint32 and weights (tokens, K) float32. */
 SC_API int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_t* idx_offset, size_t* weight_offset);
+
+/* No counterpart in strata-mlx: an addition for callers that cannot allocate device memory.
+ *
+ * sc_moe_decode_layer without a workspace argument. Some hosts of this library own every byte of device memory
+ * from start-up and hand a kernel library nothing but the inputs and outputs of each call: a serving process
+ * with a fixed memory plan that forbids allocation once it runs, or a binding from a language that has no CUDA
+ * allocator at all. Such a caller cannot supply the scratch sc_moe_decode_layer needs. This entry point takes
+ * its scratch from a static device array inside the library instead, and calls no allocator of any kind.
+ *
+ * Limit: the layer's sc_moe_decode_workspace(layer, tokens) must not exceed SC_NOALLOC_SCRATCH_BYTES (4 MiB);
+ * larger calls are rejected with SC_ERR_SCRATCH and enqueue nothing. Every GPU that loads the library holds this
+ * array until the process exits. The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream capture begins. All calls on a
+ * device share the one array and it keeps the last call's contents (the call clears what must start at zero):
+ * calls whose work overlaps on the GPU (on different streams, or from several threads) race on it and must not
+ * be issued. Same results as sc_moe_decode_layer, bit for bit. */
+#define SC_NOALLOC_SCRATCH_BYTES (4u << 20)
+SC_API int sc_moe_decode_layer_noalloc(const sc_moe_layer* layer, const void* x, int tokens, void* out, void* stream);
 
 #ifdef __cplusplus
 }

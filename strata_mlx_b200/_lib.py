@@ -25,7 +25,7 @@ ABI_VERSION = 1
 
 ERRORS = {-1: "SC_ERR_KIND", -2: "SC_ERR_SHAPE", -3: "SC_ERR_DTYPE", -4: "SC_ERR_ALIGN", -5: "SC_ERR_ARG",
           -6: "SC_ERR_CUDA", -7: "SC_ERR_WORKSPACE", -8: "SC_ERR_UNSUPPORTED", -9: "SC_ERR_TIMEOUT",
-          -10: "SC_ERR_INDEX"}
+          -10: "SC_ERR_INDEX", -11: "SC_ERR_SCRATCH"}
 
 # every symbol include/strata_cuda.h declares, with its ctypes signature
 _P, _I, _I64, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
@@ -50,6 +50,7 @@ SIGNATURES = {
     "sc_moe_decode_layer": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_workspace": (_SZ, [_P, _I]),
     "sc_moe_decode_routes": (_I, [_P, _I, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "sc_moe_decode_layer_noalloc": (_I, [_P, _P, _I, _P, _P]),
 }
 
 
@@ -99,7 +100,7 @@ def check(rc: int, what: str) -> None:
     if rc == 0:
         return
     msg = f"{what}: {ERRORS.get(rc, rc)} ({lib().sc_error_string(rc).decode()})"
-    if rc in (-1, -2, -3, -4, -5, -7):
+    if rc in (-1, -2, -3, -4, -5, -7, -11):
         raise ValueError(msg)
     raise StrataError(msg)
 

@@ -18,6 +18,7 @@ extern "C" const char* sc_error_string(int code) {
     case SC_ERR_UNSUPPORTED: return "a combination this build does not take";
     case SC_ERR_TIMEOUT: return "a kernel gave up a bounded wait";
     case SC_ERR_INDEX: return "an expert id is not below the number of experts";
+    case SC_ERR_SCRATCH: return "the call needs more than the library's static scratch (SC_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown error code";
   }
 }
