@@ -1,0 +1,64 @@
+// Shared declarations of the three-kernel decode block (decode_layer.cu) and its caller (moe.cu).
+#pragma once
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace sc {
+namespace dl {
+
+constexpr int MAXT = 8;                // tokens in a window: the N of the m16n8k16 product
+constexpr int RB = 4;                  // gate/up rows a block owns of every unit
+constexpr int RC = 16;                 // down rows a block owns of every unit (one m16 tile)
+constexpr int MAXU = 132;              // units: up to 8 x 16 routed experts + the shared one
+constexpr int MAX_ROUTER_CHUNKS = 16;  // hidden sizes up to 16 x 256
+
+// A unit is an expert the window chose (or the shared expert, unit 0) with the tokens that chose it.
+struct Unit {
+  int expert;        // -1 for the shared expert
+  uint32_t tokmask;  // bit t: token t goes through this unit
+  uint32_t kpack;    // 4 bits per token: the rank (k) of this expert among the token's choices
+  int pad;
+};
+
+struct Plan {
+  int units;
+  int pad[3];
+  Unit unit[MAXU];
+};
+
+struct LayerDev {
+  const uint8_t *gate, *up, *down, *sgate, *sup, *sdown;
+  const __half *router, *shared_gate;
+  const void* x;
+  void* out;
+  int* err;
+  int* ticket;
+  float *logits, *gsh;
+  uint32_t* idx;
+  float* wts;
+  Plan* plan;
+  void* h;
+  int T, H, I, Is, E, K, hstride;
+  int64_t rb_gu, rb_d, rb_sgu, rb_sd;
+  int gu_stride, gu_stage, gu_stages, dn_stage, dn_stages;
+};
+
+}  // namespace dl
+
+struct V2Offsets {
+  size_t err, ticket, logits, gsh, idx, wts, plan, h;
+};
+
+// h rows of the down product are padded by 32 elements so that the tokens' rows fall on different banks
+inline int v2_hstride(const sc_moe_layer* L) { return std::max(L->inter, L->shared_inter) + 32; }
+inline size_t v2_h_bytes(const sc_moe_layer* L, int tokens) {
+  return size_t(tokens * L->top_k + 1) * size_t(tokens) * size_t(v2_hstride(L)) * 2;
+}
+
+bool v2_takes(const sc_moe_layer* L, int tokens);
+int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t* ws, const V2Offsets& o,
+           cudaStream_t s);
+
+}  // namespace sc

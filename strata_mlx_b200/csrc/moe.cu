@@ -4,6 +4,9 @@
 // combine. Nothing waits on the host; the chain can be captured in a CUDA graph.
 #include <algorithm>
 
+#include <cstdlib>
+
+#include "decode_layer.cuh"
 #include "matvec.cuh"
 #include "route.cuh"
 
@@ -24,8 +27,10 @@ __global__ void moe_combine_kernel(const T* __restrict__ y, const float* __restr
   out[i] = from_f32<T>(combine_one<T>(yk, w + int64_t(t) * k, k, gt, st));
 }
 
+// The workspace: a header both paths share (error word, ticket, logits, the shared expert's gate logits, the routes,
+// the plan), then the chain's buffers or the three-kernel path's h, whichever is larger.
 struct MoeWs {
-  size_t err, logits, idx, w, g, zeros, h, y, hs, sh, gg, gu, total;
+  size_t err, ticket, logits, w, g, idx, plan, zeros, h, y, hs, sh, gg, gu, h2, total;
 };
 
 static MoeWs moe_ws(const sc_moe_layer* L, int tokens) {
@@ -35,10 +40,13 @@ static MoeWs moe_ws(const sc_moe_layer* L, int tokens) {
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o += (bytes + 255) & ~size_t(255); return at; };
   m.err = take(16);
+  m.ticket = take(16);
   m.logits = take(T * E * 4);
+  m.g = take(T * 4);
   m.idx = take(T * K * 4);
   m.w = take(T * K * 4);
-  m.g = take(T * 4);
+  m.plan = take(sizeof(dl::Plan));
+  const size_t tail = o;
   m.zeros = take(T * 4);
   m.h = take(T * K * I * es);
   m.y = take(T * K * H * es);
@@ -47,8 +55,18 @@ static MoeWs moe_ws(const sc_moe_layer* L, int tokens) {
   const bool split_gu = L->kind_gate != L->kind_up || (Is && L->kind_sgate != L->kind_sup);
   m.gg = split_gu ? take(T * K * std::max(I, Is) * es) : 0;
   m.gu = split_gu ? take(T * K * std::max(I, Is) * es) : 0;
-  m.total = o;
+  const size_t chain_end = o;
+  o = tail;
+  m.h2 = take(v2_h_bytes(L, tokens));
+  m.total = std::max(chain_end, o);
   return m;
+}
+
+// SC_DECODE_CHAIN=1 in the environment sends every layer through the chain of single-purpose kernels (the
+// reference composition), so that the two paths can be compared
+static bool chain_forced() {
+  const char* v = std::getenv("SC_DECODE_CHAIN");
+  return v && v[0] == '1';
 }
 
 static int check_layer(const sc_moe_layer* L, int tokens) {
@@ -107,6 +125,10 @@ extern "C" int sc_moe_decode_layer(const sc_moe_layer* L, const void* x, int tok
   if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!chain_forced() && v2_takes(L, tokens)) {
+    const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2};
+    return v2_run(L, x, tokens, out, ws, o, s);
+  }
   int* err = reinterpret_cast<int*>(ws + m.err);
   float* logits = reinterpret_cast<float*>(ws + m.logits);
   uint32_t* idx = reinterpret_cast<uint32_t*>(ws + m.idx);
@@ -115,7 +137,7 @@ extern "C" int sc_moe_decode_layer(const sc_moe_layer* L, const void* x, int tok
   uint32_t* zeros = reinterpret_cast<uint32_t*>(ws + m.zeros);
   const int T = tokens, K = L->top_k, E = L->experts, H = L->hidden, I = L->inter, Is = L->shared_inter;
   const int pairs = T * K;
-  if (cudaMemsetAsync(ws, 0, m.idx, s) != cudaSuccess) return SC_ERR_CUDA;  // error word + logits
+  if (cudaMemsetAsync(ws, 0, m.idx, s) != cudaSuccess) return SC_ERR_CUDA;  // error word, ticket, logits
   if (cudaMemsetAsync(zeros, 0, size_t(T) * 4, s) != cudaSuccess) return SC_ERR_CUDA;
   if (int rc = sc_router(L->router, E, H, x, L->dtype, T, logits, stream)) return rc;
   if (Is)

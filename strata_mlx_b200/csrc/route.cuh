@@ -63,7 +63,7 @@ __device__ __forceinline__ void warp_topk(const float* __restrict__ logits, int 
   float v[PER];
   uint64_t taken = 0;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) v[i] = (i * 32 + lane < n) ? logits[i * 32 + lane] : -INFINITY;
+  for (int i = 0; i < PER; ++i) v[i] = (i * 32 + lane < n) ? __ldcg(logits + i * 32 + lane) : -INFINITY;
   float sel[TOPK_MAX_K];
   uint32_t who[TOPK_MAX_K];
   for (int r = 0; r < k; ++r) {

@@ -69,6 +69,7 @@ def test_the_end_of_the_moe_block_is_the_oracles_bits(cuda, tokens, dt, nd):
 
 
 def _layer(kinds, seed, hidden=2048, inter=512, experts=64, shared=512):
+    kinds = tuple(kinds)
     rng = np.random.default_rng(seed)
     L = layer_numpy(rng, hidden, inter, experts, kinds, shared_inter=shared)
     W = {k: R.dequantize(L[k], kind, shp) for k, kind, shp in (
@@ -78,9 +79,10 @@ def _layer(kinds, seed, hidden=2048, inter=512, experts=64, shared=512):
     return L, W
 
 
-@pytest.mark.parametrize("kinds", [("Q2_0", "Q2_0", "Q2_0"), ("IQ3_S", "IQ3_S", "IQ3_S"), ("IQ3_S", "IQ3_S", "Q2_0")])
+@pytest.mark.parametrize("kinds", [("Q2_0", "Q2_0", "Q2_0"), ("IQ3_S", "IQ3_S", "IQ3_S"), ("IQ3_S", "IQ3_S", "Q2_0"),
+                                   ("IQ4_NL", "IQ4_NL", "IQ2_S")])
 @pytest.mark.parametrize("tokens", [1, 5])
-def test_the_decode_block_is_the_oracles(cuda, kinds, tokens):
+def test_the_decode_block_is_the_oracles(cuda, monkeypatch, kinds, tokens):
     """Router, top-10, softmax, routed SwiGLU experts, shared expert, combine: config-2 shapes with 64 experts."""
     L, W = _layer(kinds, tokens)
     experts, hidden, inter = 64, 2048, 512
@@ -95,6 +97,9 @@ def test_the_decode_block_is_the_oracles(cuda, kinds, tokens):
         ("sup", kinds[1], (1, 512, hidden)), ("sdown", kinds[2], (1, hidden, 512)))}
     layer = F.MoEDecodeLayer(dev(L["router"]), lin["gate"], lin["up"], lin["down"], 10,
                              shared=(lin["sgate"], lin["sup"], lin["sdown"]), shared_gate=dev(L["shared_gate"]))
+    fused = layer(x).float().cpu().numpy()  # the three-kernel path where the block types have fragment decoders
+    assert np.abs(fused - want).max() <= 2e-2 * np.abs(want).max()
+    monkeypatch.setenv("SC_DECODE_CHAIN", "1")  # the chain of single-purpose kernels
     got = layer(x).float().cpu().numpy()
     idx, w = layer.routes(tokens, x.device)
     torch.cuda.synchronize()
@@ -105,4 +110,4 @@ def test_the_decode_block_is_the_oracles(cuda, kinds, tokens):
                          F.SharedExpert(lin["sgate"], lin["sup"], lin["sdown"]), dev(L["shared_gate"]), 10)
     got2 = routed(x).float().cpu().numpy()
     assert np.abs(got2 - want).max() <= 2e-2 * np.abs(want).max()
-    np.testing.assert_array_equal(got2, got)  # the Python block and the C call give the same bits
+    np.testing.assert_array_equal(got2, got)  # the Python block and the C chain give the same bits
