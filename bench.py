@@ -166,43 +166,51 @@ def build_layers(n_layers: int, mode: str, rank: int, device):
     return layers
 
 
-def time_gate_up(layers, graph, device, reps: int) -> dict:
-    """The routed experts' fused gate/up kernel alone: one launch per layer with the routes that layer chose for
-    the last token, 48 launches captured in a graph, timed with CUDA events on the graph's stream."""
-    from strata_mlx_b200 import _lib
-    from strata_mlx_b200._lib import KINDS, ptr
+def stage_bytes(kind: str) -> dict:
+    """Algorithmic bytes of each of the three kernels of one layer, one token: every byte a kernel must read or
+    write once (routed experts: 10 distinct, one token)."""
+    rb_h, rb_i = row_bytes(kind, H), row_bytes(kind, I)
+    units = K + 1  # the routed experts and the shared one
+    h_bytes = units * (I + 32) * 2
+    return {
+        "route": E * H * 2 + H * 2 + H * 2 + E * 4,
+        "gate_up": K * 2 * I * rb_h + 2 * IS * rb_h + H * 2 + h_bytes,
+        "down": K * H * rb_i + H * row_bytes(kind, IS) + h_bytes + H * 2 + K * 8,
+    }
 
-    lib = _lib.lib()
-    outs = [torch.empty((K, I), dtype=torch.bfloat16, device=device) for _ in layers]
-    routes = [l.routes(1, device)[0].clone() for l in layers]
-    err = _lib.error_word(device)
+
+def time_stages(layers, graph, device, reps: int, capture: bool) -> dict:
+    """Each of the fused path's three kernels alone: one launch per layer on the workspace the last step left,
+    48 launches (with their programmatic dependencies) replayed as a graph, timed with CUDA events on its stream."""
     s = torch.cuda.Stream(device=device)
+    outs = [torch.empty((1, H), dtype=torch.bfloat16, device=device) for _ in layers]
+    result = {}
+    for stage, name in enumerate(("route", "gate_up", "down")):
+        def launch_all():
+            for l, o in zip(layers, outs):
+                l.stage(graph.x, o, stage)
 
-    def launch_all():
-        for l, o, r in zip(layers, outs, routes):
-            g, u = l.lin["gate"], l.lin["up"]
-            rc = lib.sc_expert_gate_up(KINDS[l.kind], ptr(g.blocks), ptr(u.blocks), E, I, H, ptr(r), K, K, ptr(graph.x),
-                                       2, ptr(o), ptr(err), s.cuda_stream)
-            _lib.check(rc, "gate_up")
-
-    with torch.cuda.stream(s):
-        launch_all()
-    s.synchronize()
-    cg = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(cg, stream=s):
-        launch_all()
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            cg.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(s)
-        for _ in range(reps):
-            cg.replay()
-        e1.record(s)
-    s.synchronize()
-    ms = e0.elapsed_time(e1) / (reps * len(layers))
-    bytes_per = sum(2 * K * I * row_bytes(l.kind, H) + H * 2 + K * I * 2 for l in layers) / len(layers)
-    return {"ms_per_launch": ms, "bytes_per_launch": bytes_per}
+        with torch.cuda.stream(s):
+            launch_all()
+        s.synchronize()
+        cg = None
+        if capture:
+            cg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cg, stream=s):
+                launch_all()
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                cg.replay() if cg else launch_all()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                cg.replay() if cg else launch_all()
+            e1.record(s)
+        s.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * len(layers))
+        nbytes = sum(stage_bytes(l.kind)[name] for l in layers) / len(layers)
+        result[name] = {"us_per_launch": ms * 1e3, "bytes_per_launch": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9}
+    return result
 
 
 def read_traffic(kinds: list) -> float | None:
@@ -314,6 +322,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--kinds", default="mixed", choices=["mixed", "Q2_0", "IQ3_S"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch the layers one by one instead of replaying a CUDA graph (for profilers that cannot "
+                         "follow a stream capture); the same kernels run")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args.gpus)
@@ -331,7 +342,7 @@ def main() -> None:
     _lib.load()
     device = torch.device("cuda", torch.cuda.current_device())
     layers = build_layers(args.layers, args.kinds, rank, device)
-    graph = F.DecodeGraph(layers, tokens=1, device=device)
+    graph = F.DecodeGraph(layers, tokens=1, device=device, capture=not args.no_graph)
     gen = torch.Generator(device=device)
     gen.manual_seed(99 + rank)
     n_tok = args.steps + args.warmup
@@ -369,10 +380,11 @@ def main() -> None:
         graph(host_x[(args.warmup + i) % n_tok])
     e2e_ms = reduce_max((time.perf_counter() - t0) / e2e_steps * 1000.0, world)
 
-    # ---- the dominant kernel alone
-    gu = time_gate_up(layers, graph, device, reps=50)
+    # ---- the three kernels alone; the dominant one (gate/up: two thirds of the expert bytes) is the roofline's
+    st = time_stages(layers, graph, device, reps=20 if args.no_graph else 50, capture=not args.no_graph)
+    gu = st["gate_up"]
     pk = peaks()
-    achieved = gu["bytes_per_launch"] / (gu["ms_per_launch"] * 1e-3) / 1e9
+    achieved = gu["gbs"]
     traffic = read_traffic([l.kind for l in layers])
 
     line = {"metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -381,12 +393,15 @@ def main() -> None:
             "config": workload_config(args, world),
             "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
                     "api": "strata_mlx_b200.fused.DecodeGraph.__call__"},
-            "roofline": {"bound": "hbm", "kernel": "mv_kernel GATEUP (routed experts' fused gate/up matvec)",
+            "roofline": {"bound": "hbm", "kernel": "gate_up_kernel (routed + shared experts' gate/up/swiglu)",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                          "peak_source": pk["source"], "traffic": traffic,
-                         "bytes_per_launch": gu["bytes_per_launch"], "us_per_launch": gu["ms_per_launch"] * 1e3},
+                         "bytes_per_launch": gu["bytes_per_launch"], "us_per_launch": gu["us_per_launch"]},
+            "kernels": st,
+            "expert_bytes_per_step": sum(stage_bytes(l.kind)["gate_up"] + stage_bytes(l.kind)["down"] for l in layers),
             "expert_matvec_gbs": achieved, "expert_matvec_frac_of_8tbs": achieved / 8000.0,
-            "gpu_launches": 8 * args.layers, "clocks": clk}
+            "gpu_launches": 3 * args.layers, "clocks": clk}
+    line["chain_gbs"] = (line["expert_bytes_per_step"] + sum(stage_bytes(l.kind)["route"] for l in layers)) / (ms * 1e-3) / 1e9
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cb = cpu_sample(args.kinds, 12.0, True)
         cpu_ms = step_seconds(cb["per_layer_s"], args.layers, args.kinds) * 1000.0

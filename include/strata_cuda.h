@@ -172,6 +172,13 @@ SC_API size_t sc_moe_decode_workspace(const sc_moe_layer* layer, int tokens);
 /* Offsets in the workspace of the last call's routes: idx (tokens, K) uint32 and weights (tokens, K) float32. */
 SC_API int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_t* idx_offset, size_t* weight_offset);
 
+/* One of the three kernels of sc_moe_decode_layer's fused path -- stage 0 routes (router, top-k, plan), 1 the
+ * experts' gate/up, 2 the down products and the combine -- on a workspace that a previous sc_moe_decode_layer call
+ * with the same layer and token count filled. For timing and profiling the kernels one at a time (no counterpart
+ * in strata-mlx). SC_ERR_UNSUPPORTED when the layer does not take the fused path. */
+SC_API int sc_moe_decode_stage(const sc_moe_layer* layer, const void* x, int tokens, void* out, void* workspace,
+                               size_t workspace_bytes, int stage, void* stream);
+
 /* No counterpart in strata-mlx: an addition for callers that cannot allocate device memory.
  *
  * sc_moe_decode_layer without a workspace argument. Some hosts of this library own every byte of device memory

@@ -9,7 +9,7 @@ namespace sc {
 namespace dl {
 
 constexpr int MAXT = 8;                // tokens in a window: the N of the m16n8k16 product
-constexpr int RB = 4;                  // gate/up rows a block owns of every unit
+constexpr int RG = 16;                 // gate/up rows of a block (one unit's m16 tile)
 constexpr int RC = 16;                 // down rows a block owns of every unit (one m16 tile)
 constexpr int MAXU = 132;              // units: up to 8 x 16 routed experts + the shared one
 constexpr int MAX_ROUTER_CHUNKS = 16;  // hidden sizes up to 16 x 256
@@ -42,7 +42,7 @@ struct LayerDev {
   void* h;
   int T, H, I, Is, E, K, hstride;
   int64_t rb_gu, rb_d, rb_sgu, rb_sd;
-  int gu_stride, gu_stage, gu_stages, dn_stage, dn_stages;
+  int dn_stage, dn_stages;
 };
 
 }  // namespace dl
@@ -58,7 +58,8 @@ inline size_t v2_h_bytes(const sc_moe_layer* L, int tokens) {
 }
 
 bool v2_takes(const sc_moe_layer* L, int tokens);
+// stage -1: the three kernels; 0, 1, 2: route, gate_up or down alone
 int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t* ws, const V2Offsets& o,
-           cudaStream_t s);
+           cudaStream_t s, int stage = -1);
 
 }  // namespace sc

@@ -131,7 +131,7 @@ __device__ __forceinline__ void stage_x_permuted(const T* __restrict__ x, int to
   const int groups = cols / 8;
   for (int i = tid; i < tokens * groups; i += nthreads) {
     const int tok = i / groups, gidx = i % groups;
-    const uint4 v = *reinterpret_cast<const uint4*>(x + int64_t(tok) * cols + 8 * gidx);
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(x + int64_t(tok) * cols + 8 * gidx));  // another kernel's output
     uint4 o;
     o.x = __byte_perm(v.x, v.z, 0x5410);  // (0, 4)
     o.y = __byte_perm(v.x, v.z, 0x7632);  // (1, 5)

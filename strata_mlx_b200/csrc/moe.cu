@@ -106,6 +106,17 @@ extern "C" int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_
   return SC_OK;
 }
 
+extern "C" int sc_moe_decode_stage(const sc_moe_layer* L, const void* x, int tokens, void* out, void* workspace,
+                                   size_t workspace_bytes, int stage, void* stream) {
+  if (int rc = check_layer(L, tokens)) return rc;
+  if (!x || !out || stage < 0 || stage > 2) return SC_ERR_ARG;
+  const MoeWs m = moe_ws(L, tokens);
+  if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
+  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2};
+  return v2_run(L, x, tokens, out, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), stage);
+}
+
 // gate/up/swiglu of one set of experts: fused when gate and up share a block type, else two products and a swiglu
 static int gate_up(int kind_g, const void* g, int kind_u, const void* u, int experts, int rows, int cols,
                    const uint32_t* idx, int pairs, int share, const void* x, int dtype, void* h, void* tmp_g,

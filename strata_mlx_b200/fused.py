@@ -205,6 +205,25 @@ class MoEDecodeLayer:
               "sc_moe_decode_layer")
         return out.reshape(x.shape)
 
+    def stage(self, x: torch.Tensor, out: torch.Tensor, stage: int) -> None:
+        """One of the fused path's three kernels (0 route, 1 gate/up, 2 down + combine) on the workspace a
+        previous call with this token count filled: for timing and profiling the kernels one at a time."""
+        xs = x.reshape(-1, self.hidden)
+        tokens = xs.shape[0]
+        ws = self.workspace(tokens, x.device)
+        check(_lib.lib().sc_moe_decode_stage(self.layer_ref(), ptr(xs), tokens, ptr(out), ptr(ws), ws.numel(), stage,
+                                             stream()), "sc_moe_decode_stage")
+
+    def check_errors(self) -> None:
+        """Reads (synchronizing) and clears the error words of this layer's workspaces; raises when a kernel
+        recorded one (a bad expert id, or a bounded wait that gave up)."""
+        for ws in self._ws.values():
+            v = int(ws[:4].view(torch.int32).item())
+            if v:
+                ws[:4].zero_()
+                raise _lib.StrataError(f"a kernel recorded {_lib.ERRORS.get(v, v)}: "
+                                       f"{_lib.lib().sc_error_string(v).decode()}")
+
     def routes(self, tokens: int, device) -> tuple:
         """(idx (tokens, K) uint32, weights (tokens, K) float32) of the last call with `tokens` tokens."""
         import ctypes
@@ -224,8 +243,8 @@ class DecodeGraph:
     in, runs every layer, and returns the last layer's output on the host. `layers` each take the previous
     layer's input when `chain` is False (each layer reads the window itself), or the previous output when True."""
 
-    def __init__(self, layers: list, tokens: int, device=None, chain: bool = False):
-        self.layers, self.tokens, self.chain = layers, tokens, chain
+    def __init__(self, layers: list, tokens: int, device=None, chain: bool = False, capture: bool = True):
+        self.layers, self.tokens, self.chain, self.capture = layers, tokens, chain, capture
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         H, dt = layers[0].hidden, layers[0].dtype
         self.x = torch.zeros((tokens, H), dtype=dt, device=dev)
@@ -235,12 +254,13 @@ class DecodeGraph:
         for l in layers:
             l.workspace(tokens, dev)
         self.stream = torch.cuda.Stream(device=dev)
-        self.graph = torch.cuda.CUDAGraph()
+        self.graph = torch.cuda.CUDAGraph() if capture else None
         with torch.cuda.stream(self.stream):
             self.run_layers()  # warm: kernel attributes are set outside the capture
         self.stream.synchronize()
-        with torch.cuda.graph(self.graph, stream=self.stream):
-            self.run_layers()
+        if capture:
+            with torch.cuda.graph(self.graph, stream=self.stream):
+                self.run_layers()
 
     def run_layers(self) -> None:
         x = self.x
@@ -250,15 +270,19 @@ class DecodeGraph:
                 x = o
 
     def replay(self) -> torch.Tensor:
-        """Runs the graph on the activations already in self.x (device-resident); returns the last output."""
-        self.graph.replay()
+        """Runs the graph on the activations already in self.x (device-resident); returns the last output. Without
+        capture (for profilers that cannot follow a stream capture) the layers are launched one by one."""
+        if self.graph is None:
+            self.run_layers()
+        else:
+            self.graph.replay()
         return self.outs[-1]
 
     def __call__(self, x_host: torch.Tensor) -> torch.Tensor:
         s = torch.cuda.current_stream()
         self.host_in.copy_(x_host.reshape(self.host_in.shape))
         self.x.copy_(self.host_in, non_blocking=True)
-        self.graph.replay()
+        self.replay()
         self.host_out.copy_(self.outs[-1], non_blocking=True)
         s.synchronize()
         return self.host_out

@@ -59,6 +59,7 @@ def test_the_three_kernel_block_is_the_oracles(cuda, kinds, tokens, dt):
     again = layer(x)
     torch.cuda.synchronize()
     _lib.check_device_errors()
+    layer.check_errors()
     assert torch.equal(got, again), "two calls on the same window gave different bits"
     want, widx, ww = oracle(L, W, x.float().cpu().numpy(), 10, nd, 512)
     idx, w = layer.routes(tokens, x.device)
