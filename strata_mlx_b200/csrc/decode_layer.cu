@@ -29,6 +29,36 @@ constexpr int WARPS = 8;                        // gate/up: eight warps along th
 constexpr int DN_WARPS = 16;                    // down: sixteen consumer warps, each taking whole units
 constexpr int DN_THREADS = (DN_WARPS + 1) * 32;  // and a producer warp
 constexpr int MAX_STAGES = 32;
+constexpr int RT_WARPS = 16;                    // route: a router row per warp; the last block's top-k uses all 16
+constexpr int RT_THREADS = RT_WARPS * 32;
+
+// Phase stamps for a profiling build (-DSC_TRACE): %globaltimer per kernel, block and phase. Compiled out otherwise.
+#ifdef SC_TRACE
+__device__ unsigned long long g_trace[3][8192][8];
+#define TRACE_POINT(k, p)                                                    \
+  do {                                                                       \
+    if (threadIdx.x == 0) {                                                  \
+      unsigned long long t_;                                                 \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                  \
+      if (blockIdx.x < 8192) g_trace[k][blockIdx.x][p] = t_;                 \
+    }                                                                        \
+  } while (0)
+#define TRACE_WARP(k, p)                                                     \
+  do {                                                                       \
+    if ((threadIdx.x & 31) == 0) {                                           \
+      unsigned long long t_;                                                 \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                  \
+      g_trace[k][4096 + (threadIdx.x >> 5)][p] = t_;                         \
+    }                                                                        \
+  } while (0)
+#else
+#define TRACE_POINT(k, p) \
+  do {                    \
+  } while (0)
+#define TRACE_WARP(k, p) \
+  do {                   \
+  } while (0)
+#endif
 
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -93,20 +123,31 @@ __device__ __forceinline__ void warp_select(uint32_t (&kv)[PER], uint32_t (&iv)[
   }
 }
 
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(128) route_kernel(LayerDev L) {
+__global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
+  TRACE_POINT(0, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int row = blockIdx.x * 4 + warp;  // router rows 0 .. E-1; row E is the shared expert's gate
+  const int row = blockIdx.x * RT_WARPS + warp;  // router rows 0 .. E-1; row E is the shared expert's gate
   const int H = L.H, E = L.E, K = L.K, T_ = L.T;
   const __half* wrow = row < E ? L.router + int64_t(row) * H : (row == E && L.Is > 0 ? L.shared_gate : nullptr);
   const int chunks = H / 256;  // 16-byte chunks a lane reads
-  uint4 w[MAX_ROUTER_CHUNKS];
+  // the first PRE chunks are fetched before the wait; more would spill at 128 registers a thread
+  constexpr int PRE = 8;
+  const uint4* wv = reinterpret_cast<const uint4*>(wrow) + lane;
+  uint4 w[PRE];
   if (wrow) {
 #pragma unroll
-    for (int c = 0; c < MAX_ROUTER_CHUNKS; ++c)
-      if (c < chunks) w[c] = __ldg(reinterpret_cast<const uint4*>(wrow) + lane + 32 * c);
+    for (int c = 0; c < PRE; ++c)
+      if (c < chunks) w[c] = __ldg(wv + 32 * c);
   }
   pdl_wait();  // the window's activations are the previous kernel's output
+  TRACE_POINT(0, 1);
   // only now may the gate/up kernel start: it reads the activations before it waits on this kernel
   pdl_launch_dependents();
   if (wrow) {
@@ -114,8 +155,9 @@ __global__ void __launch_bounds__(128) route_kernel(LayerDev L) {
       const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const T*>(L.x) + int64_t(t) * H);
       float acc = 0.f;
 #pragma unroll
-      for (int c = 0; c < MAX_ROUTER_CHUNKS; ++c)
+      for (int c = 0; c < PRE; ++c)
         if (c < chunks) acc += dot8_half<T>(w[c], __ldcg(xr + lane + 32 * c));
+      for (int c = PRE; c < chunks; ++c) acc += dot8_half<T>(__ldg(wv + 32 * c), __ldcg(xr + lane + 32 * c));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
       if (lane == 0) {
@@ -126,61 +168,152 @@ __global__ void __launch_bounds__(128) route_kernel(LayerDev L) {
   }
   __shared__ int s_last;
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    s_last = atomicAdd(L.ticket, 1) == int(gridDim.x) - 1;
-  }
+  TRACE_POINT(0, 2);
+  if (tid == 0) s_last = atomic_add_acq_rel(L.ticket, 1) == int(gridDim.x) - 1;  // release this block's logits
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
+  TRACE_POINT(0, 3);
 
-  // ---- the last block. Top-k of each token: each warp selects among a quarter of the logits, one merges the four.
-  constexpr int PER = 8;  // logits a lane holds of its warp's quarter (E <= 1024)
-  __shared__ uint32_t c_k[MAXT][4][TOPK_MAX_K], c_i[MAXT][4][TOPK_MAX_K];
-  __shared__ uint32_t s_idx[MAXT * TOPK_MAX_K];
+  // ---- the last block: top-k of each token. Every step is a few dependent operations across all lanes: a long
+  // chain of dependent shuffles or selection rounds in one warp costs microseconds here.
+  // A. warp w takes the logits [seg w, seg w + seg) (seg 32 or 64, one or two a lane) and their maximum;
+  // B. theta = the K-th largest of the warps' maxima (0 when fewer than K warps hold logits): K warps each hold a
+  //    logit >= theta, so every logit of the top K is >= theta;
+  // C. the logits >= theta (usually a few more than K) are gathered into a short list;
+  // D. warp t ranks token t's list by broadcast reads of it, keeps the K best in order (ties to the lower index,
+  //    as the reference's argpartition + sort) and takes their softmax. A list longer than CAP (many ties) falls
+  //    back to K rounds of selection over all the logits.
+  constexpr int CAP = 128;
+  constexpr uint32_t NONE = 0xffffffffu;
+  __shared__ uint32_t w_max[MAXT][RT_WARPS], s_theta[MAXT], s_cnt[MAXT];
+  __shared__ __align__(16) uint32_t m_k[MAXT][CAP], m_i[MAXT][CAP];
+  __shared__ uint32_t s_key[MAXT * TOPK_MAX_K], s_idx[MAXT * TOPK_MAX_K];
   __shared__ float s_w[MAXT * TOPK_MAX_K];
   __shared__ uint32_t s_bits[32], s_pre[32], s_mask[MAXU], s_kpack[MAXU];
   __shared__ int s_expert[MAXU];
-  const int seg = (E + 3) / 4;
-  for (int t = 0; t < T_; ++t) {
-    uint32_t kv[PER], iv[PER];
+  const int seg = E > RT_WARPS * 32 ? 64 : 32;
+  const int live = int(ceil_div(E, seg));  // warps with logits
+  const int base = seg * warp;
+  const bool ok0 = warp < live && base + lane < E, ok1 = warp < live && seg == 64 && base + 32 + lane < E;
+  uint32_t k0[MAXT], k1[MAXT];  // keys of invalid slots are 0, below every non-NaN logit's key
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int j = warp * seg + i * 32 + lane;
-      const bool ok = i * 32 + lane < seg && j < E;
-      kv[i] = ok ? fkey(__ldcg(L.logits + int64_t(t) * E + j)) : 0u;
-      iv[i] = ok ? uint32_t(j) : 0xffffffffu;
-    }
-    warp_select<PER>(kv, iv, K, lane, c_k[t][warp], c_i[t][warp]);
+  for (int t = 0; t < MAXT; ++t) {
+    k0[t] = ok0 && t < T_ ? fkey(__ldcg(L.logits + int64_t(t) * E + base + lane)) : 0u;
+    k1[t] = ok1 && t < T_ ? fkey(__ldcg(L.logits + int64_t(t) * E + base + 32 + lane)) : 0u;
   }
+  TRACE_WARP(0, 0);
+#pragma unroll
+  for (int t = 0; t < MAXT; ++t) {
+    const uint32_t mx = __reduce_max_sync(0xffffffffu, max(k0[t], k1[t]));
+    if (lane == 0 && t < T_) w_max[t][warp] = mx;
+  }
+  if (tid < MAXT) s_cnt[tid] = 0;
   for (int i = tid; i < 32; i += blockDim.x) s_bits[i] = 0;
   for (int u = tid; u < MAXU; u += blockDim.x) {
     s_mask[u] = 0;
     s_kpack[u] = 0;
   }
   __syncthreads();
-  for (int t = warp; t < T_; t += 4) {  // merge the 4 x K candidates: lane l holds candidates l and l + 32
-    uint32_t kv[2], iv[2];
+  if (warp < T_) {  // B, warp t for token t: lane l < live ranks warp l's maximum among the live warps' maxima
+    const int t = warp;
+    const uint32_t v = lane < live ? w_max[t][lane] : 0u;
+    int r = 0;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = lane + 32 * h;
-      const bool ok = c < 4 * K;
-      kv[h] = ok ? c_k[t][c / K][c % K] : 0u;
-      iv[h] = ok ? c_i[t][c / K][c % K] : 0xffffffffu;
+    for (int j = 0; j < RT_WARPS; ++j) {
+      const uint32_t a = j < live ? w_max[t][j] : 0u;
+      r += a > v || (a == v && j < lane);
     }
-    __shared__ uint32_t m_k[4][TOPK_MAX_K];
-    warp_select<2>(kv, iv, K, lane, m_k[warp], s_idx + t * K);
+    const uint32_t th = __reduce_max_sync(0xffffffffu, lane < live && r == K - 1 ? v : 0u);
+    if (lane == 0) s_theta[t] = th;
+  }
+  __syncthreads();
+  TRACE_WARP(0, 1);
+#pragma unroll
+  for (int t = 0; t < MAXT; ++t) {  // C
+    if (t >= T_) break;
+    const uint32_t th = s_theta[t];
+    const bool in0 = ok0 && k0[t] >= th, in1 = ok1 && k1[t] >= th;
+    const uint32_t b0 = __ballot_sync(0xffffffffu, in0), b1 = __ballot_sync(0xffffffffu, in1);
+    if (b0 | b1) {
+      int at = 0;
+      if (lane == 0) at = atomicAdd(&s_cnt[t], __popc(b0) + __popc(b1));
+      at = __shfl_sync(0xffffffffu, at, 0);
+      const int p0 = at + __popc(b0 & ((1u << lane) - 1u)), p1 = at + __popc(b0) + __popc(b1 & ((1u << lane) - 1u));
+      if (in0 && p0 < CAP) {
+        m_k[t][p0] = k0[t];
+        m_i[t][p0] = uint32_t(base + lane);
+      }
+      if (in1 && p1 < CAP) {
+        m_k[t][p1] = k1[t];
+        m_i[t][p1] = uint32_t(base + 32 + lane);
+      }
+    }
+  }
+  __syncthreads();
+  TRACE_POINT(0, 6);
+  for (int t = warp; t < T_; t += RT_WARPS) {  // D
+    const int m = int(s_cnt[t]);
+    TRACE_WARP(0, 2);
+    if (m <= CAP) {
+      // lane l ranks entries l, l + 32, ... of the list; four partial counts keep the chains short
+      const int nq = (m + 31) / 32;
+#pragma unroll
+      for (int q = 0; q < CAP / 32; ++q) {
+        if (q >= nq) break;
+        const bool in = lane + 32 * q < m;
+        const uint32_t kc = in ? m_k[t][lane + 32 * q] : 0u, ic = in ? m_i[t][lane + 32 * q] : NONE;
+        TRACE_WARP(0, 3);
+        int r4[4] = {0, 0, 0, 0};
+        for (int j = 0; j < m; j += 4) {  // entries past m hold stale values: masked by j + e < m
+          const uint4 a = *reinterpret_cast<const uint4*>(&m_k[t][j]);
+          const uint4 ai = *reinterpret_cast<const uint4*>(&m_i[t][j]);
+          const uint32_t av[4] = {a.x, a.y, a.z, a.w}, aiv[4] = {ai.x, ai.y, ai.z, ai.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) r4[e] += j + e < m && (av[e] > kc || (av[e] == kc && aiv[e] < ic));
+        }
+        const int r = r4[0] + r4[1] + r4[2] + r4[3];
+        if (in && r < K) {
+          s_key[t * K + r] = kc;
+          s_idx[t * K + r] = ic;
+        }
+      }
+    } else {
+      // K rounds over all the logits, each taking the best that comes after the previous pick in the order
+      uint32_t pk = 0, pi = NONE;
+      for (int rr = 0; rr < K; ++rr) {
+        uint32_t bk = 0, bi = NONE;
+        for (int j = lane; j < E; j += 32) {
+          const uint32_t kj = fkey(__ldcg(L.logits + int64_t(t) * E + j));
+          const bool after = pi == NONE || kj < pk || (kj == pk && uint32_t(j) > pi);
+          if (after && (bi == NONE || kj > bk)) {  // j ascends: an equal key keeps the lower index
+            bk = kj;
+            bi = uint32_t(j);
+          }
+        }
+        const uint32_t who = warp_best(bi == NONE ? 0u : bk, bi, pk);
+        pi = who;
+        if (lane == 0) {
+          s_key[t * K + rr] = pk;
+          s_idx[t * K + rr] = who;
+        }
+      }
+    }
     __syncwarp();
+    TRACE_WARP(0, 4);
     // softmax over the chosen logits (fused.py:491), lane k taking choice k
-    const float lk = lane < K ? unkey(m_k[warp][lane]) : -INFINITY;
-    const float top = unkey(m_k[warp][0]);
-    const float e = lane < K ? expf(lk - top) : 0.f;
+    const float top = unkey(s_key[t * K]);
+    const float e = lane < K ? expf(unkey(s_key[t * K + lane]) - top) : 0.f;
     float sum = e;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane < K) s_w[t * K + lane] = e / sum;
+    TRACE_WARP(0, 5);
+#ifdef SC_TRACE
+    if (lane == 0) g_trace[0][4200 + t][0] = uint32_t(m);
+#endif
   }
   __syncthreads();
+  TRACE_POINT(0, 4);
   const int P = T_ * K;
   for (int p = tid; p < P; p += blockDim.x) {  // the distinct experts as bits of a bitmap (E <= 1024)
     L.idx[p] = s_idx[p];
@@ -221,6 +354,7 @@ __global__ void __launch_bounds__(128) route_kernel(LayerDev L) {
   if (tid == 0) {
     L.plan->units = units;
     *L.ticket = 0;  // ready for the next call on this workspace
+    TRACE_POINT(0, 5);
   }
 }
 
@@ -247,6 +381,7 @@ __host__ __device__ inline GuSmem gu_smem(int tokens, int H, int64_t rb) {
 
 template <int KIND, typename T>
 __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
+  TRACE_POINT(1, 0);
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T_ = L.T, H = L.H;
@@ -280,6 +415,7 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   // the window's activations are complete once the route kernel let this kernel start (it waits before it does)
   stage_x_permuted<T>(static_cast<const T*>(L.x), T_, H, xs, H + 32, tid, blockDim.x);
   pdl_wait();  // the routes
+  TRACE_POINT(1, 1);
   // only now may the down kernel start: it reads the routes and the plan before it waits on this kernel
   pdl_launch_dependents();
   __shared__ Unit s_unit;
@@ -308,6 +444,8 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   const uint8_t* ub = wu + (g + 8) * rb;
   float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
   if (!mbar_wait(bar, 0, L.err)) return;
+  TRACE_POINT(1, 3);
+#pragma unroll 4
   for (int n = n0; n < n1; ++n) {
     uint4 xv = make_uint4(0, 0, 0, 0);
     if (g < T_) xv = *reinterpret_cast<const uint4*>(xs + g * (H + 32) + 32 * n + 8 * t);
@@ -331,6 +469,7 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
       accu[2] = fmaf(sb, d[2], accu[2]); accu[3] = fmaf(sb, d[3], accu[3]);
     }
   }
+  TRACE_POINT(1, 4);
   // red[value][warp][lane]: the reducing thread (value q, lane L) reads eight consecutive words
   red[((0 + 0) * WARPS + warp) * 32 + lane] = accg[0];
   red[((0 + 1) * WARPS + warp) * 32 + lane] = accg[1];
@@ -382,6 +521,7 @@ __host__ __device__ inline DnSmem dn_smem(int tokens, int K, int stage_bytes, in
 
 template <int KIND, typename T>
 __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
+  TRACE_POINT(2, 0);
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T_ = L.T, K = L.K, H = L.H;
@@ -413,6 +553,7 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   for (int i = tid; i < T_ * K; i += blockDim.x) wts[i] = __ldcg(L.wts + i);
   for (int i = tid; i < T_; i += blockDim.x) wts[T_ * K + i] = L.Is > 0 ? __ldcg(L.gsh + i) : -INFINITY;
   __syncthreads();
+  TRACE_POINT(2, 1);
   const int units = plan->units;
   // the down rows of the first units do not wait for the gate/up kernel; their h does
   auto weights = [&](int u, int s) {
@@ -431,6 +572,7 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
     }
   }
   pdl_wait();  // h
+  TRACE_POINT(2, 2);
 
   if (warp == DN_WARPS) {  // ---- producer: h of the first units, then the ring's later units whole
     if (lane == 0) {
@@ -482,6 +624,7 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
     const uint8_t* ra = st + g * rb;
     const uint8_t* rbp = st + (g + 8) * rb;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
     for (int n = 0; n < runs; ++n) {
       uint4 xv = make_uint4(0, 0, 0, 0);
       if (mine) xv = *reinterpret_cast<const uint4*>(hs + g * L.hstride + 32 * n + 8 * t);
@@ -505,16 +648,19 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
       }
     }
   }
+  TRACE_POINT(2, 3);
   named_sync(1, DN_WARPS * 32);
+  TRACE_POINT(2, 4);
   // ---- moe_combine for rows [r0, r0 + 16) of every token
   for (int i = tid; i < T_ * RC; i += DN_WARPS * 32) {
     const int tok = i / RC, m = i % RC;
-    float yk[TOPK_MAX_K];
-    for (int k = 0; k < K; ++k) yk[k] = ys[(tok * (K + 1) + k) * RC + m];
-    const float sv = L.Is > 0 ? ys[(tok * (K + 1) + K) * RC + m] : 0.f;
+    const float* yk = ys + tok * (K + 1) * RC + m;  // routed output k at yk[k * RC]
+    const float sv = L.Is > 0 ? yk[K * RC] : 0.f;
     const float gv = L.Is > 0 ? round_to<T>(wts[T_ * K + tok]) : -INFINITY;
-    static_cast<T*>(L.out)[int64_t(tok) * H + r0 + m] = from_f32<T>(combine_one<T>(yk, wts + tok * K, K, gv, sv));
+    static_cast<T*>(L.out)[int64_t(tok) * H + r0 + m] =
+        from_f32<T>(combine_one<T, RC>(yk, wts + tok * K, K, gv, sv));
   }
+  TRACE_POINT(2, 5);
 }
 
 // ---------------------------------------------------------------------------------------------------- host
@@ -559,10 +705,10 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
     if (cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, dn_total) != cudaSuccess) return SC_ERR_CUDA;
     dn_set = dn_total;
   }
-  const int grid_r = int(ceil_div(L.E + 1, 4));
+  const int grid_r = int(ceil_div(L.E + 1, RT_WARPS));
   const int grid_g = max_units * int(ceil_div(std::max(L.I, L.Is), RG));
   const int grid_d = L.H / RC;
-  if ((stage < 0 || stage == 0) && launch_pdl(kr, grid_r, 128, 0, s, L) != cudaSuccess) return SC_ERR_CUDA;
+  if ((stage < 0 || stage == 0) && launch_pdl(kr, grid_r, RT_THREADS, 0, s, L) != cudaSuccess) return SC_ERR_CUDA;
   if ((stage < 0 || stage == 1) && launch_pdl(kg, grid_g, WARPS * 32, gu_total, s, L) != cudaSuccess) return SC_ERR_CUDA;
   if ((stage < 0 || stage == 2) && launch_pdl(kd, grid_d, DN_THREADS, dn_total, s, L) != cudaSuccess) return SC_ERR_CUDA;
   return SC_OK;
@@ -570,12 +716,23 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
 
 }  // namespace dl
 
+#ifdef SC_TRACE
+extern "C" SC_API int sc_trace_read(void* host) {
+  return cudaMemcpyFromSymbol(host, dl::g_trace, sizeof(dl::g_trace)) == cudaSuccess ? 0 : -1;
+}
+extern "C" SC_API int sc_trace_clear() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, dl::g_trace) != cudaSuccess) return -1;
+  return cudaMemset(p, 0, sizeof(dl::g_trace)) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 // Whether the three-kernel path takes the layer, and the scratch it needs beyond the common header.
 bool v2_takes(const sc_moe_layer* L, int tokens) {
   auto mma_kind = [](int k) { return k == SC_Q2_0 || k == SC_IQ3_S || k == SC_IQ3_XXS; };
   if (L->dtype != SC_BF16 && L->dtype != SC_F16) return false;
   if (tokens < 1 || tokens > dl::MAXT || L->top_k > TOPK_MAX_K || tokens * L->top_k > dl::MAXU - 1) return false;
-  if (L->experts > 1024) return false;  // four top-k segments of at most 256 logits
+  if (L->experts > 1024) return false;  // the last route block's sixteen warps take 64 logits each
   if (!mma_kind(L->kind_gate) || L->kind_up != L->kind_gate || !mma_kind(L->kind_down)) return false;
   if (L->shared_inter > 0 && (L->kind_sgate != L->kind_gate || L->kind_sup != L->kind_gate || L->kind_sdown != L->kind_down))
     return false;

@@ -112,13 +112,13 @@ __device__ __forceinline__ void warp_topk(const float* __restrict__ logits, int 
 // One output of moe_combine (strata_mlx/fused.py:448-462): the k products y_k * w_k, each rounded to float32
 // before it is added (contraction off), summed as MLX's col_reduce sums them (8 partials, partial j taking
 // k = j, j + 8, ...; then the partials in order), rounded to T; plus T(T(sigmoid(g)) * s). Returns the value
-// before the final rounding to T.
-template <typename T>
+// before the final rounding to T. y_k is at y[k * YSTRIDE].
+template <typename T, int YSTRIDE = 1>
 __device__ __forceinline__ float combine_one(const float* y, const float* w, int k, float g, float s) {
   float acc = 0.f;
   for (int j = 0; j < 8 && j < k; ++j) {
     float part = 0.f;
-    for (int q = j; q < k; q += 8) part = __fadd_rn(__fmul_rn(y[q], w[q]), part);
+    for (int q = j; q < k; q += 8) part = __fadd_rn(__fmul_rn(y[q * YSTRIDE], w[q]), part);
     acc = j == 0 ? part : __fadd_rn(part, acc);
   }
   const float routed = round_to<T>(acc);
