@@ -137,9 +137,15 @@ SC_API size_t sc_tiles_of_workspace(int experts);
 /* strata_mlx/blocks.py:516-536 tile_matmul(blocks, kind, shape, a, tile_expert): c (P, rows) float32 =
  * W[tile_expert[p / 16]] . a[p] for a (P, cols) of a_dtype, P a multiple of 16; the weights are rounded to
  * a_dtype before they multiply; float32 sums. Tiles naming no expert (>= experts) are left unwritten.
- * bfloat16 / float16 `a` run on the tcgen05 tensor cores; float32 `a` on the CUDA cores. */
+ * bfloat16 / float16 `a` run on the tcgen05 tensor cores; float32 `a` on the CUDA cores. err: device int that
+ * records SC_ERR_TIMEOUT when one of the tensor-core kernel's bounded waits gives up (may be NULL). */
 SC_API int sc_tile_matmul(int kind, const void* blocks, int experts, int rows, int cols, const void* a, int a_dtype, int P,
-                   const uint32_t* tile_expert, float* c, void* stream);
+                   const uint32_t* tile_expert, float* c, int* err, void* stream);
+/* Which kernel sc_tile_matmul runs for these arguments: 1 the tcgen05 tensor-core kernel (float16 / bfloat16 `a`,
+ * rows by 128, cols by 256, at most 4096 tiles, 16-byte aligned `a` and blocks), 0 the CUDA-core kernel. No
+ * counterpart in strata-mlx (its tile kernel is one Metal kernel). */
+SC_API int sc_tile_matmul_path(int kind, int experts, int rows, int cols, int a_dtype, int P, const void* a,
+                               const void* blocks);
 
 /* One MoE block in decode, strata_mlx/fused.py:487-497 (_Routed.__call__): the router (fused.py:377-390), top_k
  * (:424-436), the softmax over the chosen logits (:491), the routed SwiGLU experts (blocks.py:801-829), the

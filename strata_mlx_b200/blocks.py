@@ -222,7 +222,8 @@ def tile_matmul(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Tensor, 
     aa = _contig(a)
     out = torch.empty((p, rows), dtype=torch.float32, device=a.device)
     check(_lib.lib().sc_tile_matmul(_kind(kind), ptr(_contig(blocks)), experts, rows, cols, ptr(aa), _dtype(aa), p,
-                                    ptr(te), ptr(out), stream()), f"tile_matmul {kind} {tuple(shape)}")
+                                    ptr(te), ptr(out), ptr(_lib.error_word(a.device)), stream()),
+          f"tile_matmul {kind} {tuple(shape)}")
     return out
 
 

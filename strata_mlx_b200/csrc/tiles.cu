@@ -152,8 +152,13 @@ extern "C" int sc_tiles_of(const void* idx, int idx_dtype, int pairs, int k, int
   return cudaGetLastError() == cudaSuccess ? SC_OK : SC_ERR_CUDA;
 }
 
+extern "C" int sc_tile_matmul_path(int kind, int experts, int rows, int cols, int a_dtype, int P, const void* a,
+                                   const void* blocks) {
+  return tile_mma_takes(kind, experts, rows, cols, a_dtype, P, a, blocks) ? 1 : 0;
+}
+
 extern "C" int sc_tile_matmul(int kind, const void* blocks, int experts, int rows, int cols, const void* a, int a_dtype,
-                              int P, const uint32_t* tile_expert, float* c, void* stream) {
+                              int P, const uint32_t* tile_expert, float* c, int* err, void* stream) {
   if (!blocks || !a || !tile_expert || !c || experts < 1 || P < 0) return SC_ERR_ARG;
   if (block_info(kind).per_block == 0) return SC_ERR_KIND;
   if (!tileable(kind, rows, cols) || P % TOKENS_TILE) return SC_ERR_SHAPE;
@@ -162,7 +167,7 @@ extern "C" int sc_tile_matmul(int kind, const void* blocks, int experts, int row
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a_dtype != SC_F32) {
     const int rc = tile_mma_launch(kind, static_cast<const uint8_t*>(blocks), experts, rows, cols, rb, a, a_dtype, P,
-                                   tile_expert, c, s);
+                                   tile_expert, c, err, s);
     if (rc != SC_ERR_UNSUPPORTED) return rc;
   }
   int rc = SC_ERR_DTYPE;

@@ -59,7 +59,7 @@ def test_bad_arguments_are_rejected_before_any_launch():
     assert lib.sc_router(fake, 8, 12, fake, 0, 1, fake, None) == -4  # cols not a multiple of 8
     assert lib.sc_top_k(fake, 1, 8, 17, fake, None) == -2  # k above 16
     assert lib.sc_tiles_of(fake, 0, 10, 2, 4, fake, fake, fake, None, 0, None) == -7
-    assert lib.sc_tile_matmul(0, fake, 4, 100, 128, fake, 1, 16, fake, fake, None) == -2  # rows not by 64
+    assert lib.sc_tile_matmul(0, fake, 4, 100, 128, fake, 1, 16, fake, fake, None, None) == -2  # rows not by 64
     assert lib.sc_moe_decode_workspace(None, 1) == 0
 
 
@@ -77,3 +77,16 @@ def test_products_refuse_tensors_off_the_gpu():
         blocks.BlockSwitchLinear(b, "Q2_0", (1, 4, 64))
     with pytest.raises(ValueError, match="CUDA"):
         blocks.dequantize(b, "Q2_0", (4, 64))
+
+
+def test_which_kernel_takes_a_tile_product():
+    """bfloat16 / float16 at rows by 128 and columns by 256 go to the tcgen05 kernel; the rest to the CUDA cores."""
+    lib = _lib.lib()
+    k = _lib.KINDS["IQ3_XXS"]
+    aligned = ctypes.c_void_p(1 << 20)
+    assert lib.sc_tile_matmul_path(k, 512, 512, 2048, 2, 32768, aligned, aligned) == 1
+    assert lib.sc_tile_matmul_path(k, 512, 2048, 512, 1, 32768, aligned, aligned) == 1
+    assert lib.sc_tile_matmul_path(k, 512, 512, 2048, 0, 32768, aligned, aligned) == 0  # float32
+    assert lib.sc_tile_matmul_path(k, 512, 64, 2048, 2, 32768, aligned, aligned) == 0  # rows not by 128
+    assert lib.sc_tile_matmul_path(k, 512, 512, 2048, 2, 16 * 5000, aligned, aligned) == 0  # too many tiles
+    assert lib.sc_tile_matmul_path(k, 512, 512, 2048, 2, 32768, ctypes.c_void_p((1 << 20) + 8), aligned) == 0
