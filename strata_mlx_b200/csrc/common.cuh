@@ -161,6 +161,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return true;
 }
 
+// mbar_wait for warps that share their SM with others doing the work: each try_wait may suspend the thread for
+// up to `hint_ns` (it wakes when the phase completes), so a waiting warp takes no issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err,
+                                                long long limit = 2000000000LL, uint32_t hint_ns = 1000000) {
+  if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait_sleep(bar, parity, hint_ns)) {
+    if (clock64() - start > limit) {
+      record_error(err, SC_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // One-dimensional bulk copy global -> this block's shared memory, completing `bytes` on `bar`.
 // dst and src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -14,8 +14,9 @@ from strata_mlx_b200.synthetic import blocks_numpy
 
 pytestmark = pytest.mark.gpu
 
-# 256-, 64- and 32-weight blocks; Q8_0's wide rows take the kernel's two-raw-stage layout
-KINDS = ["IQ3_XXS", "Q2_0", "IQ3_S", "IQ4_NL", "Q8_0"]
+# 256-, 64- and 32-weight blocks; rows of 1024 columns of IQ3_XXS, IQ3_S and IQ2_XXS start at two offsets
+# modulo 16 bytes (two raw boxes a chunk)
+KINDS = ["IQ3_XXS", "Q2_0", "IQ3_S", "IQ4_NL", "IQ2_XXS"]
 
 
 def dev(a):
@@ -52,6 +53,24 @@ def test_the_tensor_core_product_is_the_product_with_rounded_weights(cuda, kind,
     ok = np.repeat(te < experts, 16)
     err = np.abs(got[ok] - want[ok]).max() / np.abs(want[ok]).max()
     assert err <= 1e-5, err  # float32 sums in the tensor cores' order
+
+
+@pytest.mark.parametrize("kind, cols", [("IQ3_XXS", 512), ("IQ3_XXS", 256), ("IQ2_XXS", 512)])
+def test_rows_whose_chunks_start_at_four_or_eight_offsets(cuda, kind, cols):
+    """Rows of 196, 98 and 132 bytes: their chunks start at 4, 8 and 4 different offsets modulo 16 bytes."""
+    rng = np.random.default_rng(5)
+    experts, rows = 24, 256
+    data = blocks_numpy(kind, experts, rows, cols, rng, uniform=0.01)
+    w = R.dequantize(data, kind, (experts, rows, cols))
+    te = tile_list(rng, experts, 12)
+    a = dev(rng.standard_normal((16 * len(te), cols)).astype(np.float32)).to(torch.bfloat16)
+    got = B.tile_matmul(dev(data), kind, (experts, rows, cols), a, dev(te))
+    torch.cuda.synchronize()
+    _lib.check_device_errors()
+    want = R.tile_matmul(w, a.float().cpu().numpy(), te, "bfloat16")
+    ok = np.repeat(te < experts, 16)
+    got = got.cpu().numpy()
+    assert np.abs(got[ok] - want[ok]).max() <= 1e-5 * np.abs(want[ok]).max()
 
 
 def test_a_call_with_no_expert_tiles_writes_nothing(cuda):
