@@ -132,14 +132,25 @@ __device__ __forceinline__ uint32_t instr_desc(int n) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(BM >> 4) << 24);
 }
 
-// D (tensor memory) (+)= A (tensor memory, 128 lanes x 16 values) . B (shared memory)^T
+// D (tensor memory) (+)= A (tensor memory, 128 lanes x 16 values) . B (shared memory)^T; no output lane disabled
+// (the form with the disable-output-lane operand issued faster than the form without it, measured here)
 __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(p));
+  return p != 0;
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -440,39 +451,48 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---- MMA issuer
-    if (lane == 0) {
-      uint32_t bc = 0, jc = 0, ic = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < items && ok && !*bail; item += gridDim.x, ++ic) {
-        const uint32_t g = groups[item / RB];
-        const int nt = int((g >> 12) & 15) + 1;
-        const int b = int(ic & 1);
-        if (!(ok = mbar_wait(&acc_empty[b], ((ic >> 1) & 1) ^ 1, err))) break;
-        TT(5, ic);
-        tc_fence_after();
-        const uint32_t d = tmem + uint32_t(ACC_COL + b * NMAX);
-        const uint32_t idesc = instr_desc<T>(nt * TOKENS_TILE);
-        for (int j = 0; j < KC && ok; ++j, ++jc) {
-          const int wr = int(jc & 1);
-          for (int i = 0; i < CHK / SUBK; ++i) {
-            const int bs = int(bc % BSTAGES);
-            if (!(ok = mbar_wait(&w_full[wr * 4 + i], (jc >> 1) & 1, err))) break;
-            if (!(ok = mbar_wait(&b_full[bs], (bc / BSTAGES) & 1, err))) break;
-            TT(4, bc);
-            tc_fence_after();
-            const uint32_t a = tmem + uint32_t(WCOL + wr * 128 + i * 32);
-            const uint64_t bd = smem_desc(bst + bs * B_STAGE);
+    // ---- MMA issuer: the whole warp follows the loop and waits (a wait that gives up in any lane ends the loop in
+    // all of them); one elected lane issues. All 512 columns are
+    // this block's, so tensor memory starts at address 0: the MMAs' addresses are loop constants.
+    const bool leader = elect_one();
+    uint32_t bc = 0, jc = 0, ic = 0;
+    bool ok = tmem == 0;
+    if (!ok) record_error(err, SC_ERR_CUDA);
+    for (int item = blockIdx.x; item < items && ok && !*bail; item += gridDim.x, ++ic) {
+      const uint32_t g = groups[item / RB];
+      const int nt = int((g >> 12) & 15) + 1;
+      const int b = int(ic & 1);
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_empty[b], ((ic >> 1) & 1) ^ 1, err)))) break;
+      if (leader) TT(5, ic);
+      tc_fence_after();
+      const uint32_t d = uint32_t(ACC_COL + b * NMAX);
+      const uint32_t idesc = instr_desc<T>(nt * TOKENS_TILE);
+      for (int j = 0; j < KC && ok; ++j, ++jc) {
+        const int wr = int(jc & 1);
+        for (int i = 0; i < CHK / SUBK; ++i) {
+          const int bs = int(bc % BSTAGES);
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&w_full[wr * 4 + i], (jc >> 1) & 1, err)))) break;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&b_full[bs], (bc / BSTAGES) & 1, err)))) break;
+          if (leader) TT(4, bc);
+          tc_fence_after();
+          const uint32_t a = uint32_t(WCOL + wr * 128 + i * 32);
+          const uint64_t bd = smem_desc(bst + bs * B_STAGE);
+          if (leader) {
 #pragma unroll
             for (int k = 0; k < SUBK / 16; ++k) mma_ts(d, a + 8 * k, bd + 2 * k, idesc, (j | i | k) != 0);
             mma_commit(&b_empty[bs]);
-            ++bc;
           }
-          if (ok) mma_commit(&w_empty[wr]);
+          __syncwarp();
+          ++bc;
         }
-        if (ok) mma_commit(&acc_full[b]);
+        if (ok && leader) mma_commit(&w_empty[wr]);
+        __syncwarp();
       }
-      if (!ok) *bail = 1;
+      if (ok && leader) mma_commit(&acc_full[b]);
+      __syncwarp();
+    }
+    if (!ok) *bail = 1;
+    if (leader) {
       mma_commit(done);  // arrives once every MMA this thread issued has finished
       mbar_wait(done, 0, nullptr, 20000000LL);
     }
