@@ -166,6 +166,142 @@ def build_layers(n_layers: int, mode: str, rank: int, device):
     return layers
 
 
+def build_ep_layers(n_layers: int, mode: str, rank: int, world: int, device):
+    """The chain's layers, expert parallel: every rank makes the same model (the seeds do not depend on the rank)
+    and keeps its share of each layer's routed experts; the router and shared expert are replicated."""
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import ep as EP
+    from strata_mlx_b200.synthetic import blocks_cuda
+
+    e0, e1 = EP.expert_range(rank, world, E)
+    layers = []
+    for l in range(n_layers):
+        kind = kind_of(l, mode)
+        seed = 10 * l
+        g = torch.Generator(device=device)
+        g.manual_seed(seed + 7)
+        mine = {}
+        for name, shp, sd in (("gate", (E, I, H), 1), ("up", (E, I, H), 2), ("down", (E, H, I), 3)):
+            full = blocks_cuda(kind, *shp, seed + sd, device)
+            mine[name] = B.BlockSwitchLinear(EP.local_experts(full, E, rank, world), kind, (e1 - e0,) + shp[1:])
+            del full
+        shared = tuple(B.BlockSwitchLinear(blocks_cuda(kind, 1, r, c, seed + sd, device), kind, (1, r, c))
+                       for r, c, sd in ((IS, H, 4), (IS, H, 5), (H, IS, 6)))
+        router = (torch.randn((E, H), generator=g, device=device) * 0.02).half()
+        sgw = (torch.randn((H,), generator=g, device=device) * 0.02).half()
+        layer = EP.EPMoEDecodeLayer(router, mine["gate"], mine["up"], mine["down"], K, E, shared=shared,
+                                    shared_gate=sgw, dtype=torch.bfloat16)
+        layer.kind = kind
+        layers.append(layer)
+    torch.cuda.empty_cache()
+    return layers
+
+
+def run_ep(args, world, rank, local) -> None:
+    """N > 1: expert parallel decode, one token per rank per step through the chain; the exchange of each layer is
+    an NCCL all-gather and all-reduce (strata_mlx_b200/ep.py)."""
+    import torch.distributed as dist
+    from strata_mlx_b200 import _lib
+
+    _lib.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    layers = build_ep_layers(args.layers, args.kinds, rank, world, device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99 + rank)
+    n_tok = args.steps + args.warmup
+    xs = torch.randn((n_tok, H), generator=gen, device=device).to(torch.bfloat16)
+    x_in = torch.empty((1, H), dtype=torch.bfloat16, device=device)
+    torch.cuda.synchronize()
+
+    def eager():
+        y = x_in
+        for l in layers:
+            y = l(y)
+        return y
+
+    # the chain with its collectives captured as one CUDA graph (released before the process group ends)
+    cs = torch.cuda.Stream(device=device)
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        for i in range(3):
+            x_in.copy_(xs[i : i + 1])
+            eager()
+    torch.cuda.current_stream().wait_stream(cs)
+    torch.cuda.synchronize()
+    barrier(world)
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cs):
+            y_out = eager()
+        torch.cuda.synchronize()
+    barrier(world)
+
+    def step():
+        if graph is None:
+            return eager()
+        graph.replay()
+        return y_out
+
+    s = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        x_in.copy_(xs[i : i + 1])
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.steps):
+        x_in.copy_(xs[args.warmup + i : args.warmup + i + 1])
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = reduce_max(e0.elapsed_time(e1) / args.steps, world)
+    barrier(world)
+    _lib.check_device_errors(device)
+
+    # e2e: the public call per layer, the rank's token from pinned host memory, its result back to the host
+    host_x = xs.cpu().pin_memory()
+    e2e_steps = min(args.steps, 200)
+    for i in range(3):
+        x_in.copy_(host_x[i : i + 1], non_blocking=True)
+        step().cpu()
+    barrier(world)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        x_in.copy_(host_x[(args.warmup + i) % n_tok : (args.warmup + i) % n_tok + 1], non_blocking=True)
+        step().cpu()
+    e2e_ms = reduce_max((time.perf_counter() - t0) / e2e_steps * 1000.0, world)
+
+    # bytes a rank must read per step: its experts' share of the window's pairs (world tokens x K pairs spread over
+    # world ranks: K pairs per rank on average) plus the replicated router and shared expert
+    per_rank = sum(stage_bytes(l.kind)["gate_up"] + stage_bytes(l.kind)["down"] + stage_bytes(l.kind)["route"]
+                   for l in layers)
+    pk = peaks()
+    achieved = per_rank / (ms * 1e-3) / 1e9
+    cfg = workload_config(args, world)
+    cfg["parallelism"] = f"ep{world}: experts sharded over ranks, NCCL all-gather + all-reduce per layer"
+    line = {"metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: seeded GGUF blocks and float16 router made in HBM",
+            "config": cfg,
+            "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2,
+                    "d2h_bytes_per_step": H * 2, "api": "strata_mlx_b200.ep.EPMoEDecodeLayer.__call__ per layer"},
+            "roofline": {"bound": "hbm", "kernel": "the whole expert-parallel step of a rank (kernels + exchange)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "peak_source": pk["source"], "traffic": None},
+            "gpu_launches": 4 * args.layers, "clocks": clk}
+    line["graph"] = graph is not None
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    torch.cuda.synchronize()
+    barrier(world)
+    dist.destroy_process_group()
+
+
 def stage_bytes(kind: str) -> dict:
     """Algorithmic bytes of each of the three kernels of one layer, one token: every byte a kernel must read or
     write once (routed experts: 10 distinct, one token)."""
@@ -334,6 +470,10 @@ def main() -> None:
             import torch.distributed as dist
 
             dist.destroy_process_group()
+        return
+
+    if world > 1:
+        run_ep(args, world, rank, local)
         return
 
     from strata_mlx_b200 import _lib

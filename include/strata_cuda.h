@@ -185,6 +185,22 @@ SC_API int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_t* i
 SC_API int sc_moe_decode_stage(const sc_moe_layer* layer, const void* x, int tokens, void* out, void* workspace,
                                size_t workspace_bytes, int stage, void* stream);
 
+/* Expert parallel decode (no counterpart in strata-mlx, which runs on one device). One rank's share of an MoE block
+ * over a window of `tokens` (the window holds every rank's tokens): the router and top-k for every token, then the
+ * gate/up/down of only the pairs whose expert is in [expert_begin, expert_end); layer->gate/up/down hold just those
+ * experts (expert e at e - expert_begin), layer->experts is the total. Writes y_pairs (tokens, top_k, hidden) of the
+ * activations' type: each pair's expert output, zero for pairs of other ranks' experts, so that a sum over ranks
+ * (all-reduce) holds every pair's output exactly; the shared expert's output and the routes stay in the workspace
+ * (sc_moe_decode_workspace bytes). Takes the layers the fused decode takes; SC_ERR_UNSUPPORTED otherwise. */
+SC_API int sc_moe_decode_layer_ep(const sc_moe_layer* layer, const void* x, int tokens, int expert_begin,
+                                  int expert_end, void* y_pairs, void* workspace, size_t workspace_bytes, void* stream);
+
+/* After sc_moe_decode_layer_ep and the sum of y_pairs over ranks: moe_combine (strata_mlx/fused.py:467-481) of the
+ * window's tokens from y_pairs and the workspace's routes and shared expert output, into out (tokens, hidden). The
+ * same bits as sc_moe_decode_layer gives for those tokens on one device. */
+SC_API int sc_moe_decode_combine(const sc_moe_layer* layer, const void* y_pairs, int tokens, void* out,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* No counterpart in strata-mlx: an addition for callers that cannot allocate device memory.
  *
  * sc_moe_decode_layer without a workspace argument. Some hosts of this library own every byte of device memory

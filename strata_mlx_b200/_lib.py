@@ -52,6 +52,8 @@ SIGNATURES = {
     "sc_moe_decode_workspace": (_SZ, [_P, _I]),
     "sc_moe_decode_routes": (_I, [_P, _I, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
     "sc_moe_decode_stage": (_I, [_P, _P, _I, _P, _P, _SZ, _I, _P]),
+    "sc_moe_decode_layer_ep": (_I, [_P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
+    "sc_moe_decode_combine": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_layer_noalloc": (_I, [_P, _P, _I, _P, _P]),
 }
 

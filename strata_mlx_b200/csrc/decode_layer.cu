@@ -315,10 +315,11 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   __syncthreads();
   TRACE_POINT(0, 4);
   const int P = T_ * K;
-  for (int p = tid; p < P; p += blockDim.x) {  // the distinct experts as bits of a bitmap (E <= 1024)
+  for (int p = tid; p < P; p += blockDim.x) {  // this rank's distinct experts as bits of a bitmap (E <= 1024)
     L.idx[p] = s_idx[p];
     L.wts[p] = s_w[p];
-    atomicOr(&s_bits[s_idx[p] >> 5], 1u << (s_idx[p] & 31));
+    const int le = int(s_idx[p]) - L.e0;  // the local expert
+    if (le >= 0 && int(s_idx[p]) < L.e1) atomicOr(&s_bits[le >> 5], 1u << (le & 31));
   }
   __syncthreads();
   if (warp == 0) {  // exclusive prefix of the bitmap's popcounts
@@ -333,7 +334,9 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   }
   __syncthreads();
   for (int p = tid; p < P; p += blockDim.x) {
-    const uint32_t e = s_idx[p];
+    const int le = int(s_idx[p]) - L.e0;
+    if (le < 0 || int(s_idx[p]) >= L.e1) continue;  // another rank's expert
+    const uint32_t e = uint32_t(le);
     // unit 0 is the shared expert; the routed units follow in ascending expert order
     const int u = 1 + int(s_pre[e >> 5]) + __popc(s_bits[e >> 5] & ((1u << (e & 31)) - 1u));
     const int tok = p / K, k = p % K;
@@ -651,6 +654,19 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   TRACE_POINT(2, 3);
   named_sync(1, DN_WARPS * 32);
   TRACE_POINT(2, 4);
+  if (L.ypairs) {  // expert parallel: the pairs' outputs (zero for other ranks' experts) and the shared expert's
+    for (int i = tid; i < T_ * RC; i += DN_WARPS * 32) {
+      const int tok = i / RC, m = i % RC;
+      const float* yk = ys + tok * (K + 1) * RC + m;
+      for (int k = 0; k < K; ++k) {
+        const int e = int(__ldcg(L.idx + tok * K + k));
+        const float v = e >= L.e0 && e < L.e1 ? yk[k * RC] : 0.f;
+        static_cast<T*>(L.ypairs)[(int64_t(tok) * K + k) * H + r0 + m] = from_f32<T>(v);
+      }
+      static_cast<T*>(L.sout)[int64_t(tok) * H + r0 + m] = from_f32<T>(L.Is > 0 ? yk[K * RC] : 0.f);
+    }
+    return;
+  }
   // ---- moe_combine for rows [r0, r0 + 16) of every token
   for (int i = tid; i < T_ * RC; i += DN_WARPS * 32) {
     const int tok = i / RC, m = i % RC;
@@ -743,7 +759,7 @@ bool v2_takes(const sc_moe_layer* L, int tokens) {
 }
 
 int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t* ws, const V2Offsets& o,
-           cudaStream_t s, int stage) {
+           cudaStream_t s, int stage, const V2Ep& ep) {
   dl::LayerDev d{};
   d.gate = static_cast<const uint8_t*>(L->gate);
   d.up = static_cast<const uint8_t*>(L->up);
@@ -774,6 +790,10 @@ int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t*
   d.rb_d = row_bytes(L->kind_down, L->inter);
   d.rb_sgu = L->shared_inter ? row_bytes(L->kind_sgate, L->hidden) : 0;
   d.rb_sd = L->shared_inter ? row_bytes(L->kind_sdown, L->shared_inter) : 0;
+  d.e0 = ep.e0;
+  d.e1 = ep.e1 < 0 ? L->experts : ep.e1;
+  d.ypairs = ep.ypairs;
+  d.sout = ws + o.sout;
   int rc = SC_ERR_UNSUPPORTED;
   auto go = [&]<int KGU, int KD>() {
     if (L->dtype == SC_BF16) rc = dl::run<KGU, KD, __nv_bfloat16>(d, s, stage);

@@ -43,12 +43,23 @@ struct LayerDev {
   int T, H, I, Is, E, K, hstride;
   int64_t rb_gu, rb_d, rb_sgu, rb_sd;
   int dn_stage, dn_stages;
+  // expert parallel: this rank's experts [e0, e1) (its gate/up/down blocks hold only those, expert e at e - e0);
+  // with ypairs set, the down kernel writes each pair's expert output (T, K, H), zero for pairs of other ranks'
+  // experts, and the shared expert's (T, H) to sout, in place of the combine
+  int e0, e1;
+  void *ypairs, *sout;
 };
 
 }  // namespace dl
 
 struct V2Offsets {
-  size_t err, ticket, logits, gsh, idx, wts, plan, h;
+  size_t err, ticket, logits, gsh, idx, wts, plan, h, sout;
+};
+
+// expert parallel: rank's experts [e0, e1) and where the pairs' outputs go (null: the single-GPU combine)
+struct V2Ep {
+  int e0 = 0, e1 = -1;
+  void* ypairs = nullptr;
 };
 
 // h rows of the down product are padded by 32 elements so that the tokens' rows fall on different banks
@@ -60,6 +71,6 @@ inline size_t v2_h_bytes(const sc_moe_layer* L, int tokens) {
 bool v2_takes(const sc_moe_layer* L, int tokens);
 // stage -1: the three kernels; 0, 1, 2: route, gate_up or down alone
 int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t* ws, const V2Offsets& o,
-           cudaStream_t s, int stage = -1);
+           cudaStream_t s, int stage = -1, const V2Ep& ep = V2Ep{});
 
 }  // namespace sc

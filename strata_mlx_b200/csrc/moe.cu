@@ -30,7 +30,7 @@ __global__ void moe_combine_kernel(const T* __restrict__ y, const float* __restr
 // The workspace: a header both paths share (error word, ticket, logits, the shared expert's gate logits, the routes,
 // the plan), then the chain's buffers or the three-kernel path's h, whichever is larger.
 struct MoeWs {
-  size_t err, ticket, logits, w, g, idx, plan, zeros, h, y, hs, sh, gg, gu, h2, total;
+  size_t err, ticket, logits, w, g, idx, plan, zeros, h, y, hs, sh, gg, gu, h2, sout, total;
 };
 
 static MoeWs moe_ws(const sc_moe_layer* L, int tokens) {
@@ -58,6 +58,7 @@ static MoeWs moe_ws(const sc_moe_layer* L, int tokens) {
   const size_t chain_end = o;
   o = tail;
   m.h2 = take(v2_h_bytes(L, tokens));
+  m.sout = take(T * H * es);  // expert parallel: the shared expert's output
   m.total = std::max(chain_end, o);
   return m;
 }
@@ -113,8 +114,46 @@ extern "C" int sc_moe_decode_stage(const sc_moe_layer* L, const void* x, int tok
   const MoeWs m = moe_ws(L, tokens);
   if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
   if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
-  const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2};
+  const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
   return v2_run(L, x, tokens, out, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), stage);
+}
+
+extern "C" int sc_moe_decode_layer_ep(const sc_moe_layer* L, const void* x, int tokens, int expert_begin,
+                                      int expert_end, void* y_pairs, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+  if (int rc = check_layer(L, tokens)) return rc;
+  if (!x || !y_pairs) return SC_ERR_ARG;
+  if (expert_begin < 0 || expert_end <= expert_begin || expert_end > L->experts) return SC_ERR_SHAPE;
+  const MoeWs m = moe_ws(L, tokens);
+  if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
+  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
+  V2Ep ep;
+  ep.e0 = expert_begin;
+  ep.e1 = expert_end;
+  ep.ypairs = y_pairs;
+  return v2_run(L, x, tokens, nullptr, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), -1, ep);
+}
+
+extern "C" int sc_moe_decode_combine(const sc_moe_layer* L, const void* y_pairs, int tokens, void* out,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_layer(L, tokens)) return rc;
+  if (!y_pairs || !out) return SC_ERR_ARG;
+  const MoeWs m = moe_ws(L, tokens);
+  if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const int T = tokens, K = L->top_k, H = L->hidden, Is = L->shared_inter;
+  const int64_t n = int64_t(T) * H;
+  const float* wts = reinterpret_cast<const float*>(ws + m.w);
+  const float* g = reinterpret_cast<const float*>(ws + m.g);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bool ok = dispatch_dtype(L->dtype, [&]<typename OutT>() {
+    moe_combine_kernel<OutT><<<int(ceil_div(n, 256)), 256, 0, s>>>(
+        static_cast<const OutT*>(y_pairs), wts, Is ? g : nullptr, Is ? reinterpret_cast<const OutT*>(ws + m.sout) : nullptr,
+        T, K, H, static_cast<OutT*>(out));
+  });
+  if (!ok) return SC_ERR_DTYPE;
+  return cudaGetLastError() == cudaSuccess ? SC_OK : SC_ERR_CUDA;
 }
 
 // gate/up/swiglu of one set of experts: fused when gate and up share a block type, else two products and a swiglu
@@ -137,7 +176,7 @@ extern "C" int sc_moe_decode_layer(const sc_moe_layer* L, const void* x, int tok
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (!chain_forced() && v2_takes(L, tokens)) {
-    const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2};
+    const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
     return v2_run(L, x, tokens, out, ws, o, s);
   }
   int* err = reinterpret_cast<int*>(ws + m.err);
