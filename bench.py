@@ -302,6 +302,134 @@ def run_ep(args, world, rank, local) -> None:
     dist.destroy_process_group()
 
 
+# ---- configuration 3: the prefill grouped expert GEMM (--workload prefill)
+
+PREFILL_TOKENS, ZIPF_S = 2048, 0.8
+PREFILL_KIND = "IQ3_XXS"
+
+
+def prefill_routes():
+    """2,048 tokens' top-10 of 512 experts from logits N(0,1) - s ln(rank_e) over a seeded permutation of ranks
+    (s = 0.8: 364 experts used, as many as the reference's real layers use)."""
+    rng = np.random.default_rng(2048)
+    logits = rng.standard_normal((PREFILL_TOKENS, E)) - ZIPF_S * np.log(rng.permutation(E) + 1)
+    return np.argsort(-logits, axis=1, kind="stable")[:, :K].astype(np.int32)
+
+
+def run_prefill(args, world, rank) -> None:
+    """Configuration 3 on one GPU: a prefill chunk's 20,480 (token, expert) pairs through switch_glu's tiled
+    path (tiles_of, the gate / up / down tile products on tcgen05, swiglu), IQ3_XXS experts, bf16 in, fp32 sums.
+    `value`: TFLOP/s on the pairs' 6 * pairs * H * I flops; roofline: the gate product's kernel alone against the
+    measured bf16 tensor peak."""
+    from strata_mlx_b200 import _lib
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200.synthetic import blocks_cuda
+
+    _lib.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    kind = PREFILL_KIND
+    gate = B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, 31, device), kind, (E, I, H))
+    up = B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, 32, device), kind, (E, I, H))
+    down = B.BlockSwitchLinear(blocks_cuda(kind, E, H, I, 33, device), kind, (E, H, I))
+    idx_np = prefill_routes()
+    counts = np.bincount(idx_np.reshape(-1), minlength=E)
+    idx = torch.from_numpy(idx_np).to(device).reshape(1, PREFILL_TOKENS, K)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4)
+    x = torch.randn((1, PREFILL_TOKENS, H), generator=gen, device=device).to(torch.bfloat16)
+    pairs = PREFILL_TOKENS * K
+    flops = 6.0 * pairs * H * I
+    s = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        B.switch_glu(x, idx, up, gate, down)
+    torch.cuda.synchronize()
+    clocks = Clocks(0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        B.switch_glu(x, idx, up, gate, down)
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    _lib.check_device_errors(device)
+
+    # the gate product's kernel alone (the dominant kernel: the three products are alike in flops)
+    te, token, where = B.tiles_of(idx, E)
+    a = x.reshape(-1, H).index_select(0, token.to(torch.int64))
+    for _ in range(3):
+        B.tile_matmul(gate.blocks, kind, (E, I, H), a, te)
+    torch.cuda.synchronize()
+    reps = 20
+    e0.record(s)
+    for _ in range(reps):
+        B.tile_matmul(gate.blocks, kind, (E, I, H), a, te)
+    e1.record(s)
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    k_tflops = 2.0 * pairs * I * H / (k_ms * 1e-3) / 1e12
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk, src = float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        tpk, src = 1590.0, "fallback"
+
+    # e2e: the reference's call (switch_glu) from pinned host activations, the pairs' outputs back to the host
+    host_x = x.cpu().pin_memory()
+    e2e_steps = min(args.steps, 10)
+    out = B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down).cpu()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        out = B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down).cpu()
+    e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1000.0
+
+    line = {"metric": "prefill grouped expert GEMM TFLOP/s (config 3)", "value": flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded IQ3_XXS blocks made in HBM, seeded Zipf-skewed routes",
+            "config": {"workload": "config3: prefill grouped expert GEMM, 2048-token chunk, top-10 of 512 experts "
+                                   "(hidden 2048, SwiGLU inter 512), IQ3_XXS, bf16 in / fp32 accumulate",
+                       "pairs": pairs, "experts_used": int((counts > 0).sum()), "max_pairs_per_expert": int(counts.max()),
+                       "median_pairs_per_used_expert": float(np.median(counts[counts > 0])), "zipf_s": ZIPF_S,
+                       "flops_per_step": flops,
+                       "l2": "inputs larger than L2: 3 x 401 MB of expert blocks, 364 experts' share read per step"},
+            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": PREFILL_TOKENS * H * 2, "d2h_bytes_per_step": int(out.numel()) * 2,
+                    "api": "strata_mlx_b200.blocks.switch_glu"},
+            "roofline": {"bound": "tensor", "kernel": "tile_mma_kernel (the gate product, 512 x 2048)",
+                         "achieved": k_tflops, "peak": tpk, "unit": "TFLOP/s", "frac": k_tflops / tpk,
+                         "peak_source": src, "traffic": None, "us_per_launch": k_ms * 1e3},
+            "gpu_launches": 5, "clocks": clk}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = prefill_cpu_sample(pairs, flops)
+    print(json.dumps(line), flush=True)
+
+
+def prefill_cpu_sample(pairs: int, flops: float) -> dict:
+    """The C oracle (decode + float32 matvec per pair, all host cores) on a bounded sample of pairs of the same
+    shapes, scaled to the step's pairs."""
+    from oracle import cref
+    from strata_mlx_b200.synthetic import blocks_numpy
+
+    threads = cref.threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(3)
+    lib = cref.lib()
+    k = cref.KINDS[PREFILL_KIND]
+    w_gu = blocks_numpy(PREFILL_KIND, 1, I, H, rng)
+    w_d = blocks_numpy(PREFILL_KIND, 1, H, I, rng)
+    x = rng.standard_normal(H).astype(np.float32)
+    h = rng.standard_normal(I).astype(np.float32)
+    og, od = np.empty(I, np.float32), np.empty(H, np.float32)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0 or n < 3:
+        for w, xin, o, r, c in ((w_gu, x, og, I, H), (w_gu, x, og, I, H), (w_d, h, od, H, I)):
+            lib.ref_matvec(k, w.ctypes.data, r, c, xin.ctypes.data, o.ctypes.data)
+        n += 1
+    per_pair = (time.perf_counter() - t0) / n
+    return {"value": flops / (per_pair * pairs) / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n} pairs' gate, up and down products timed (~10 s), scaled to {pairs} pairs"}
+
+
 def stage_bytes(kind: str) -> dict:
     """Algorithmic bytes of each of the three kernels of one layer, one token: every byte a kernel must read or
     write once (routed experts: 10 distinct, one token)."""
@@ -457,6 +585,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--kinds", default="mixed", choices=["mixed", "Q2_0", "IQ3_S"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the layers one by one instead of replaying a CUDA graph (for profilers that cannot "
@@ -472,6 +602,15 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
+    if args.workload == "prefill":
+        if rank == 0:
+            run_prefill(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            barrier(world)
+            dist.destroy_process_group()
+        return
     if world > 1:
         run_ep(args, world, rank, local)
         return
