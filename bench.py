@@ -213,7 +213,15 @@ def run_ep(args, world, rank, local) -> None:
     x_in = torch.empty((1, H), dtype=torch.bfloat16, device=device)
     torch.cuda.synchronize()
 
+    chain = None
+    if len(layers) % 2 == 0 and os.environ.get("SC_EP_NCCL") != "1":
+        from strata_mlx_b200 import ep as EP
+
+        chain = EP.EPDecodeChain(layers, 1, device)  # the exchange in the kernels, over peer memory
+
     def eager():
+        if chain is not None:
+            return chain(x_in)
         y = x_in
         for l in layers:
             y = l(y)
@@ -282,23 +290,30 @@ def run_ep(args, world, rank, local) -> None:
     pk = peaks()
     achieved = per_rank / (ms * 1e-3) / 1e9
     cfg = workload_config(args, world)
-    cfg["parallelism"] = f"ep{world}: experts sharded over ranks, NCCL all-gather + all-reduce per layer"
+    cfg["parallelism"] = (f"ep{world}: experts sharded over ranks, the exchange in the kernels over peer memory "
+                          "(NVLink stores, release/acquire counts)" if chain is not None else
+                          f"ep{world}: experts sharded over ranks, NCCL all-gather + all-reduce per layer")
     line = {"metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic: seeded GGUF blocks and float16 router made in HBM",
             "config": cfg,
             "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2,
-                    "d2h_bytes_per_step": H * 2, "api": "strata_mlx_b200.ep.EPMoEDecodeLayer.__call__ per layer"},
+                    "d2h_bytes_per_step": H * 2,
+                    "api": "strata_mlx_b200.ep.EPDecodeChain.__call__" if chain is not None else
+                           "strata_mlx_b200.ep.EPMoEDecodeLayer.__call__ per layer"},
             "roofline": {"bound": "hbm", "kernel": "the whole expert-parallel step of a rank (kernels + exchange)",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                          "peak_source": pk["source"], "traffic": None},
-            "gpu_launches": 4 * args.layers, "clocks": clk}
+            "gpu_launches": 4 * args.layers + (1 if chain is not None else 0), "clocks": clk}
     line["graph"] = graph is not None
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph
     torch.cuda.synchronize()
     barrier(world)
+    if chain is not None:
+        chain.check_errors()
+        chain.close()
     dist.destroy_process_group()
 
 

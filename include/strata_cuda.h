@@ -201,6 +201,30 @@ SC_API int sc_moe_decode_layer_ep(const sc_moe_layer* layer, const void* x, int 
 SC_API int sc_moe_decode_combine(const sc_moe_layer* layer, const void* y_pairs, int tokens, void* out,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Expert parallel over peer memory (no counterpart in strata-mlx): the collectives of sc_moe_decode_layer_ep's
+ * exchange replaced by stores into the other ranks' memory over NVLink, with counts that mark each part complete.
+ * Every rank holds an exchange buffer of sc_ep_exchange_bytes bytes (zeroed once), maps the others' buffers with
+ * sc_ipc_handle / sc_ipc_open, and describes them in an sc_ep_exchange. A chain of L layers (L even) for a step:
+ * sc_ep_feed (this rank's tokens into every rank's window), then per layer l sc_moe_decode_layer_ep_p2p with
+ * parity l % 2 and sc_ep_combine (last = l == L - 1), which writes this rank's tokens' outputs to `out` and into
+ * every rank's next window. The kernels' waits on other ranks are bounded (about a second; SC_ERR_TIMEOUT). */
+typedef struct sc_ep_exchange {
+  const uint64_t* peers; /* device array (ranks): each rank's exchange buffer, mapped into this process */
+  uint64_t own;          /* this rank's exchange buffer (= peers[rank]), a device address */
+  int ranks, rank, tokens_per_rank;
+} sc_ep_exchange;
+
+SC_API size_t sc_ep_exchange_bytes(const sc_moe_layer* layer, int ranks, int tokens_per_rank);
+SC_API int sc_ipc_handle(const void* ptr, void* handle /* 64 bytes */, size_t* offset);
+SC_API int sc_ipc_open(const void* handle, void** base);
+SC_API int sc_ipc_close(void* base);
+SC_API int sc_ep_feed(const sc_moe_layer* layer, const sc_ep_exchange* ex, const void* x, void* stream);
+SC_API int sc_moe_decode_layer_ep_p2p(const sc_moe_layer* layer, const sc_ep_exchange* ex, int expert_begin,
+                                      int expert_end, int parity, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+SC_API int sc_ep_combine(const sc_moe_layer* layer, const sc_ep_exchange* ex, int parity, int last, void* out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* No counterpart in strata-mlx: an addition for callers that cannot allocate device memory.
  *
  * sc_moe_decode_layer without a workspace argument. Some hosts of this library own every byte of device memory

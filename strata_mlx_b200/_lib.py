@@ -54,8 +54,21 @@ SIGNATURES = {
     "sc_moe_decode_stage": (_I, [_P, _P, _I, _P, _P, _SZ, _I, _P]),
     "sc_moe_decode_layer_ep": (_I, [_P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_combine": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
+    "sc_ep_exchange_bytes": (_SZ, [_P, _I, _I]),
+    "sc_ipc_handle": (_I, [_P, _P, _P]),
+    "sc_ipc_open": (_I, [_P, _P]),
+    "sc_ipc_close": (_I, [_P]),
+    "sc_ep_feed": (_I, [_P, _P, _P, _P]),
+    "sc_moe_decode_layer_ep_p2p": (_I, [_P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "sc_ep_combine": (_I, [_P, _P, _I, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_layer_noalloc": (_I, [_P, _P, _I, _P, _P]),
 }
+
+
+class SCExchange(ctypes.Structure):
+    """sc_ep_exchange (include/strata_cuda.h): the ranks' exchange buffers for expert parallel over peer memory."""
+    _fields_ = [("peers", ctypes.c_void_p), ("own", ctypes.c_uint64), ("ranks", ctypes.c_int), ("rank", ctypes.c_int),
+                ("tokens_per_rank", ctypes.c_int)]
 
 
 class SCLayer(ctypes.Structure):

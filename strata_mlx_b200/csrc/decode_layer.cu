@@ -21,6 +21,7 @@
 #include "mma_decode.cuh"
 #include "route.cuh"
 #include "decode_layer.cuh"
+#include "ep.cuh"
 
 namespace sc {
 namespace dl {
@@ -148,6 +149,16 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   }
   pdl_wait();  // the window's activations are the previous kernel's output
   TRACE_POINT(0, 1);
+  if (L.peers) {  // expert parallel over peer memory: every rank's tokens are in the window once it counts full
+    if (tid == 0) {
+      const uint64_t own = L.peers[L.rank];
+      ep::wait_count(ep::at_u32(own, ep::xcount_off(L.par)), L.xtarget, L.err);
+      TRACE_POINT(0, 7);
+      // the previous layer's pair-output count: its combine has read it (it ran before this kernel's wait)
+      if (blockIdx.x == 0) *ep::at_u32(own, ep::ycount_off(L.par ^ 1)) = 0;
+    }
+    __syncthreads();
+  }
   // only now may the gate/up kernel start: it reads the activations before it waits on this kernel
   pdl_launch_dependents();
   if (wrow) {
@@ -415,7 +426,12 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   const uint32_t* grid = nullptr;
   if constexpr (KIND == SC_IQ3_S) grid = load_tabs<KIND>(smem + S.tabs).iq3s;
   if constexpr (KIND == SC_IQ3_XXS) grid = load_tabs<KIND>(smem + S.tabs).iq3xxs;
-  // the window's activations are complete once the route kernel let this kernel start (it waits before it does)
+  // the window's activations are complete once the route kernel let this kernel start (it waits before it does);
+  // over peer memory, the window's count is read here too (already full), for the peers' writes' visibility
+  if (L.peers) {
+    if (tid == 0) ep::wait_count(ep::at_u32(L.peers[L.rank], ep::xcount_off(L.par)), L.xtarget, L.err);
+    __syncthreads();
+  }
   stage_x_permuted<T>(static_cast<const T*>(L.x), T_, H, xs, H + 32, tid, blockDim.x);
   pdl_wait();  // the routes
   TRACE_POINT(1, 1);
@@ -654,6 +670,27 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   TRACE_POINT(2, 3);
   named_sync(1, DN_WARPS * 32);
   TRACE_POINT(2, 4);
+  if (L.peers) {  // expert parallel over peer memory: each pair's output to its token's rank, then count there
+    const size_t yo = ep::yoff(L.par, T_, L.tl, K, H);
+    for (int i = tid; i < T_ * RC; i += DN_WARPS * 32) {
+      const int tok = i / RC, m = i % RC;
+      const float* yk = ys + tok * (K + 1) * RC + m;
+      T* dst = reinterpret_cast<T*>(L.peers[tok / L.tl] + yo) + int64_t(tok % L.tl) * K * H + r0 + m;
+      for (int k = 0; k < K; ++k) {
+        const int e = int(__ldcg(L.idx + tok * K + k));
+        if (e >= L.e0 && e < L.e1) dst[int64_t(k) * H] = from_f32<T>(yk[k * RC]);
+      }
+      static_cast<T*>(L.sout)[int64_t(tok) * H + r0 + m] = from_f32<T>(L.Is > 0 ? yk[K * RC] : 0.f);
+    }
+    named_sync(1, DN_WARPS * 32);
+    TRACE_POINT(2, 6);
+    if (tid == 0) {
+      ep::fence_release_sys();
+      for (int g = 0; g < L.G; ++g) ep::count_relaxed(ep::at_u32(L.peers[g], ep::ycount_off(L.par)));
+    }
+    TRACE_POINT(2, 7);
+    return;
+  }
   if (L.ypairs) {  // expert parallel: the pairs' outputs (zero for other ranks' experts) and the shared expert's
     for (int i = tid; i < T_ * RC; i += DN_WARPS * 32) {
       const int tok = i / RC, m = i % RC;
@@ -794,6 +831,13 @@ int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t*
   d.e1 = ep.e1 < 0 ? L->experts : ep.e1;
   d.ypairs = ep.ypairs;
   d.sout = ws + o.sout;
+  d.peers = ep.peers;
+  d.G = ep.G;
+  d.rank = ep.rank;
+  d.tl = ep.tl;
+  d.par = ep.par;
+  d.xtarget = uint32_t(ep.G * ep::COMBINE_BLOCKS);
+  d.ytarget = uint32_t(ep.G * (L->hidden / dl::RC));
   int rc = SC_ERR_UNSUPPORTED;
   auto go = [&]<int KGU, int KD>() {
     if (L->dtype == SC_BF16) rc = dl::run<KGU, KD, __nv_bfloat16>(d, s, stage);

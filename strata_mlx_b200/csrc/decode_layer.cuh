@@ -48,6 +48,12 @@ struct LayerDev {
   // experts, and the shared expert's (T, H) to sout, in place of the combine
   int e0, e1;
   void *ypairs, *sout;
+  // expert parallel over peer memory (peers null: not in use): the ranks' exchange buffers (this rank's mappings),
+  // G ranks, this one `rank`, `tl` tokens a rank; the layer reads window X[par] and writes pair outputs Y[par];
+  // xtarget / ytarget: the counts that mark them complete
+  const uint64_t* peers;
+  int G, rank, tl, par;
+  uint32_t xtarget, ytarget;
 };
 
 }  // namespace dl
@@ -60,6 +66,8 @@ struct V2Offsets {
 struct V2Ep {
   int e0 = 0, e1 = -1;
   void* ypairs = nullptr;
+  const uint64_t* peers = nullptr;  // peer-memory exchange (see ep.cuh); ypairs unused then
+  int G = 1, rank = 0, tl = 0, par = 0;
 };
 
 // h rows of the down product are padded by 32 elements so that the tokens' rows fall on different banks

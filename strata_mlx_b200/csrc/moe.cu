@@ -7,6 +7,7 @@
 #include <cstdlib>
 
 #include "decode_layer.cuh"
+#include "ep.cuh"
 #include "matvec.cuh"
 #include "route.cuh"
 
@@ -133,6 +134,55 @@ extern "C" int sc_moe_decode_layer_ep(const sc_moe_layer* L, const void* x, int 
   ep.e1 = expert_end;
   ep.ypairs = y_pairs;
   return v2_run(L, x, tokens, nullptr, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), -1, ep);
+}
+
+extern "C" int sc_moe_decode_layer_ep_p2p(const sc_moe_layer* L, const sc_ep_exchange* ex, int expert_begin,
+                                          int expert_end, int parity, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  if (!ex || !ex->peers || !ex->own || ex->ranks < 1 || ex->rank < 0 || ex->rank >= ex->ranks ||
+      ex->tokens_per_rank < 1 || (parity != 0 && parity != 1))
+    return SC_ERR_ARG;
+  const int tokens = ex->ranks * ex->tokens_per_rank;
+  if (int rc = check_layer(L, tokens)) return rc;
+  if (expert_begin < 0 || expert_end <= expert_begin || expert_end > L->experts) return SC_ERR_SHAPE;
+  const MoeWs m = moe_ws(L, tokens);
+  if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
+  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
+  V2Ep e;
+  e.e0 = expert_begin;
+  e.e1 = expert_end;
+  e.peers = ex->peers;
+  e.G = ex->ranks;
+  e.rank = ex->rank;
+  e.tl = ex->tokens_per_rank;
+  e.par = parity;
+  const void* window = reinterpret_cast<const void*>(ex->own + ep::xoff(parity, tokens, L->hidden));
+  return v2_run(L, window, tokens, nullptr, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), -1,
+                e);
+}
+
+extern "C" int sc_ep_combine(const sc_moe_layer* L, const sc_ep_exchange* ex, int parity, int last, void* out,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ex || !ex->peers || !ex->own || ex->ranks < 1 || ex->rank < 0 || ex->rank >= ex->ranks ||
+      ex->tokens_per_rank < 1 || (parity != 0 && parity != 1) || !out)
+    return SC_ERR_ARG;
+  const int tokens = ex->ranks * ex->tokens_per_rank;
+  if (int rc = check_layer(L, tokens)) return rc;
+  const MoeWs m = moe_ws(L, tokens);
+  if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  ep::EpArgs A{};
+  A.peers = ex->peers;
+  A.G = ex->ranks, A.rank = ex->rank, A.tl = ex->tokens_per_rank, A.T = tokens;
+  A.H = L->hidden, A.K = L->top_k, A.Is = L->shared_inter, A.par = parity, A.last = last;
+  A.wts = reinterpret_cast<const float*>(ws + m.w);
+  A.gsh = reinterpret_cast<const float*>(ws + m.g);
+  A.sout = ws + m.sout;
+  A.out = out;
+  A.err = reinterpret_cast<int*>(ws + m.err);
+  A.ytarget = uint32_t(ex->ranks * (L->hidden / dl::RC));
+  return ep::combine_launch(A, L->dtype, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sc_moe_decode_combine(const sc_moe_layer* L, const void* y_pairs, int tokens, void* out,

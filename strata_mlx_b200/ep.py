@@ -12,9 +12,16 @@ A layer runs over the window of every rank's tokens:
      exactly;
   4. sc_moe_decode_combine: every token's combine, in the fixed order of moe_combine (fused.py:448-462).
 Each token's result has the bits the single-device layer gives it. Per layer the exchange carries t H values per
-rank in (all-gather) and G t K H values across ranks (all-reduce)."""
+rank in (all-gather) and G t K H values across ranks (all-reduce).
+
+EPDecodeChain runs a chain of such layers with the exchange done by the kernels themselves over peer memory (NVLink):
+each rank maps the others' exchange buffers (CUDA IPC, PeerExchange); a combine writes its tokens' outputs straight
+into every rank's next window, the down kernel writes each pair's output straight to the rank of the pair's token,
+and release / acquire counts mark the parts complete (layout in csrc/ep.cuh). No collective runs on the data path."""
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -117,3 +124,85 @@ class EPMoEDecodeLayer:
         self._sum(Y)
         out = self._combine(Y, state)
         return out[self.rank * t : (self.rank + 1) * t].reshape(x.shape)
+
+
+class PeerExchange:
+    """Every rank's exchange buffer (sc_ep_exchange_bytes for the layer's shape, zeroed) mapped into every other rank
+    by CUDA IPC; `desc` is the sc_ep_exchange the kernels take. close() unmaps the peers' buffers."""
+
+    def __init__(self, layer_struct, tokens_per_rank: int, device, group=None):
+        import torch.distributed as dist
+
+        lib = _lib.lib()
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        n = lib.sc_ep_exchange_bytes(ctypes.addressof(layer_struct), self.world, tokens_per_rank)
+        if n == 0:
+            raise ValueError("no exchange for this layer")
+        self.buf = torch.zeros(n, dtype=torch.uint8, device=device)
+        handle, off = ctypes.create_string_buffer(64), ctypes.c_size_t()
+        check(lib.sc_ipc_handle(ptr(self.buf), handle, ctypes.byref(off)), "sc_ipc_handle")
+        every = [None] * self.world
+        dist.all_gather_object(every, (bytes(handle.raw), off.value), group=group)
+        self._opened, bases = [], []
+        for r, (h, o) in enumerate(every):
+            if r == self.rank:
+                bases.append(self.buf.data_ptr())
+                continue
+            base = ctypes.c_void_p()
+            check(lib.sc_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(base)), "sc_ipc_open")
+            self._opened.append(base.value)
+            bases.append(base.value + o)
+        self.peers = torch.tensor([b if b < 2 ** 63 else b - 2 ** 64 for b in bases], dtype=torch.int64, device=device)
+        self.desc = _lib.SCExchange(self.peers.data_ptr(), self.buf.data_ptr(), self.world, self.rank, tokens_per_rank)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        for base in self._opened:
+            _lib.lib().sc_ipc_close(ctypes.c_void_p(base))
+        self._opened = []
+
+
+class EPDecodeChain:
+    """A chain of EPMoEDecodeLayer (an even number: the layers alternate the exchange's halves) run with the exchange
+    in the kernels over peer memory. Calling it with this rank's tokens (t, hidden) runs every layer and returns the
+    last layer's outputs for them; every rank of the group must call it with the same t. Bit-identical to the
+    single-device chain."""
+
+    def __init__(self, layers: list, tokens_per_rank: int, device, group=None):
+        if not layers or len(layers) % 2:
+            raise ValueError("the chain needs an even number of layers")
+        self.layers, self.t, self.device = layers, tokens_per_rank, device
+        first = layers[0]
+        self.hidden, self.dtype = first.hidden, first.dtype
+        self.ex = PeerExchange(first.base.layer, tokens_per_rank, device, group)
+        self.T = self.ex.world * tokens_per_rank
+        self.out = torch.empty((tokens_per_rank, self.hidden), dtype=self.dtype, device=device)
+        for l in layers:
+            l.base.workspace(self.T, device)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        lib = _lib.lib()
+        xs = x.reshape(self.t, self.hidden)
+        if xs.dtype != self.dtype:
+            raise ValueError(f"activations of {xs.dtype}; the chain was built for {self.dtype}")
+        xs = xs if xs.is_contiguous() else xs.contiguous()
+        d = ctypes.byref(self.ex.desc)
+        check(lib.sc_ep_feed(self.layers[0].base.layer_ref(), d, ptr(xs), stream()), "sc_ep_feed")
+        last = len(self.layers) - 1
+        for i, l in enumerate(self.layers):
+            ws = l.base.workspace(self.T, self.device)
+            ref = l.base.layer_ref()
+            check(lib.sc_moe_decode_layer_ep_p2p(ref, d, l.e0, l.e1, i % 2, ptr(ws), ws.numel(), stream()),
+                  "sc_moe_decode_layer_ep_p2p")
+            check(lib.sc_ep_combine(ref, d, i % 2, int(i == last), ptr(self.out), ptr(ws), ws.numel(), stream()),
+                  "sc_ep_combine")
+        return self.out.reshape(x.shape)
+
+    def check_errors(self) -> None:
+        for l in self.layers:
+            l.base.check_errors()
+
+    def close(self) -> None:
+        self.ex.close()

@@ -27,6 +27,7 @@ def main():
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", local)
     bad = 0
+    chain_one, chain_par = [], []
     for kinds in (("IQ3_S", "IQ3_S", "Q2_0"), ("Q2_0", "Q2_0", "IQ3_XXS")):
         L = layer_numpy(np.random.default_rng(5), H, I, E, kinds, shared_inter=S)
         cu = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in L.items()
@@ -43,6 +44,8 @@ def main():
                                shared_gate=cu["shared_gate"])
         par = EP.EPMoEDecodeLayer(cu["router"], mine["gate"], mine["up"], mine["down"], K, E, shared=shared,
                                   shared_gate=cu["shared_gate"])
+        chain_one.append(one)
+        chain_par.append(par)
         for t in (1, 2):
             x = torch.randn((t, H), generator=torch.Generator(device=dev).manual_seed(10 * rank + t), device=dev)
             x = x.to(torch.bfloat16)
@@ -53,6 +56,25 @@ def main():
                 bad += 1
                 diff = (got.float() - want.float()).abs().max().item()
                 print(f"rank {rank} {kinds} t={t}: differs from the single-device block (max {diff})", flush=True)
+    # the two layers as a chain with the exchange in the kernels (peer memory): three steps, so that the counts are
+    # reset and reused across steps
+    for t in (1, 2):
+        chain = EP.EPDecodeChain(chain_par, t, dev)
+        for step in range(3):
+            x = torch.randn((t, H), generator=torch.Generator(device=dev).manual_seed(100 * step + 10 * rank + t),
+                            device=dev).to(torch.bfloat16)
+            got = chain(x).clone()
+            want = x
+            for one in chain_one:
+                want = torch.cat([one(want[i : i + 1]) for i in range(t)])
+            torch.cuda.synchronize()
+            chain.check_errors()
+            if not torch.equal(got, want):
+                bad += 1
+                diff = (got.float() - want.float()).abs().max().item()
+                print(f"rank {rank} peer chain t={t} step {step}: differs (max {diff})", flush=True)
+        dist.barrier()
+        chain.close()
     flag = torch.tensor([bad], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
