@@ -26,7 +26,7 @@
 namespace sc {
 namespace dl {
 
-constexpr int WARPS = 8;                        // gate/up: eight warps along the columns
+constexpr int WARPS = 8;                        // gate/up: eight warps along the columns (16 made a second wave of blocks)
 constexpr int DN_WARPS = 16;                    // down: sixteen consumer warps, each taking whole units
 constexpr int DN_THREADS = (DN_WARPS + 1) * 32;  // and a producer warp
 constexpr int MAX_STAGES = 32;
