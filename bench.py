@@ -304,7 +304,8 @@ def run_ep(args, world, rank, local) -> None:
             "roofline": {"bound": "hbm", "kernel": "the whole expert-parallel step of a rank (kernels + exchange)",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                          "peak_source": pk["source"], "traffic": None},
-            "gpu_launches": 4 * args.layers + (1 if chain is not None else 0), "clocks": clk}
+            "gpu_launches": (4 * args.layers + (1 if chain is not None else 0)) * args.steps,
+            "gpu_launches_per_step": 4 * args.layers + (1 if chain is not None else 0), "clocks": clk}
     line["graph"] = graph is not None
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -390,13 +391,19 @@ def run_prefill(args, world, rank) -> None:
         tpk, src = 1590.0, "fallback"
 
     # e2e: the reference's call (switch_glu) from pinned host activations, the pairs' outputs back to the host
+    # (pinned host buffers both ways)
     host_x = x.cpu().pin_memory()
     e2e_steps = min(args.steps, 10)
-    out = B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down).cpu()
+    out = B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down)
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    host_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        out = B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down).cpu()
+        host_out.copy_(B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down), non_blocking=True)
+    torch.cuda.synchronize(device)
     e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1000.0
+    out = host_out
 
     line = {"metric": "prefill grouped expert GEMM TFLOP/s (config 3)", "value": flops / (ms * 1e-3) / 1e12,
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -414,7 +421,8 @@ def run_prefill(args, world, rank) -> None:
             "roofline": {"bound": "tensor", "kernel": "tile_mma_kernel (the gate product, 512 x 2048)",
                          "achieved": k_tflops, "peak": tpk, "unit": "TFLOP/s", "frac": k_tflops / tpk,
                          "peak_source": src, "traffic": None, "us_per_launch": k_ms * 1e3},
-            "gpu_launches": 5, "clocks": clk}
+            # per step: tiles_of, slot_pairs, the gate / up products, swiglu, the down product
+            "gpu_launches": 6 * args.steps, "gpu_launches_per_step": 6, "clocks": clk}
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = prefill_cpu_sample(pairs, flops)
     print(json.dumps(line), flush=True)
@@ -694,7 +702,7 @@ def main() -> None:
             "kernels": st,
             "expert_bytes_per_step": sum(stage_bytes(l.kind)["gate_up"] + stage_bytes(l.kind)["down"] for l in layers),
             "expert_matvec_gbs": achieved, "expert_matvec_frac_of_8tbs": achieved / 8000.0,
-            "gpu_launches": 3 * args.layers, "clocks": clk}
+            "gpu_launches": 3 * args.layers * args.steps, "gpu_launches_per_step": 3 * args.layers, "clocks": clk}
     line["chain_gbs"] = (line["expert_bytes_per_step"] + sum(stage_bytes(l.kind)["route"] for l in layers)) / (ms * 1e-3) / 1e9
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cb = cpu_sample(args.kinds, 12.0, True)

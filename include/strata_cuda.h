@@ -147,6 +147,19 @@ SC_API int sc_tile_matmul(int kind, const void* blocks, int experts, int rows, i
 SC_API int sc_tile_matmul_path(int kind, int experts, int rows, int cols, int a_dtype, int P, const void* a,
                                const void* blocks);
 
+/* strata_mlx/blocks.py:566-576 _tiled_glu in one call: the gate, up and down tile products of a prompt's pairs
+ * laid out by sc_tiles_of (tile_expert, where): gate and up stored in a_dtype by the products' epilogues, their
+ * swiglu, and the down product written straight into out (pairs, hidden) in the pairs' order, all in a_dtype
+ * (float16 / bfloat16): the same bits
+ * as three sc_tile_matmul calls, swiglu and the unsort. a (P, hidden) holds each slot's token (as _tiled_glu gathers
+ * it). SC_ERR_UNSUPPORTED when a product is not one the tcgen05 kernel takes (the caller then composes the three).
+ * workspace: sc_tile_glu_workspace(P, inter, a_dtype) bytes. */
+SC_API int sc_tile_glu(int kind_gate, const void* gate, int kind_up, const void* up, int kind_down, const void* down,
+                       int experts, int hidden, int inter, const void* a, int a_dtype, int P,
+                       const uint32_t* tile_expert, const uint32_t* where, int pairs, void* out, void* workspace,
+                       size_t workspace_bytes, int* err, void* stream);
+SC_API size_t sc_tile_glu_workspace(int P, int inter, int a_dtype);
+
 /* One MoE block in decode, strata_mlx/fused.py:487-497 (_Routed.__call__): the router (fused.py:377-390), top_k
  * (:424-436), the softmax over the chosen logits (:491), the routed SwiGLU experts (blocks.py:801-829), the
  * shared expert and its gate, and moe_combine (fused.py:467-481), for a window of 1..8 tokens. */

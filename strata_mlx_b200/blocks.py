@@ -251,9 +251,24 @@ def tiles_of(indices: torch.Tensor, experts: int) -> tuple:
 
 
 def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.Tensor:
-    """The three products of a prompt's pairs through `tile_matmul`, the pairs in tiles (blocks.py:566-576)."""
+    """The three products of a prompt's pairs through `tile_matmul`, the pairs in tiles (blocks.py:566-576). For
+    float16 / bfloat16 on the tensor-core kernel the three run as one call (sc_tile_glu: swiglu and the unsort in
+    the products' epilogues), with the same bits."""
     tiles, token, where = tiles_of(indices, gate.num_experts)
     a = x.reshape(-1, x.shape[-1]).index_select(0, token.to(torch.int64))
+    if a.dtype in (torch.float16, torch.bfloat16):
+        lib = _lib.lib()
+        p, pairs = a.shape[0], indices.numel()
+        n = lib.sc_tile_glu_workspace(p, gate.output_dims, _dtype(a))
+        ws = torch.empty(n, dtype=torch.uint8, device=a.device)
+        out = torch.empty((pairs, down.output_dims), dtype=a.dtype, device=a.device)
+        rc = lib.sc_tile_glu(_kind(gate.kind), ptr(gate.blocks), _kind(up.kind), ptr(up.blocks), _kind(down.kind),
+                             ptr(down.blocks), gate.num_experts, gate.input_dims, gate.output_dims, ptr(a), _dtype(a), p,
+                             ptr(tiles), ptr(where), pairs, ptr(out), ptr(ws), n, ptr(_lib.error_word(a.device)),
+                             stream())
+        if rc != -8:  # SC_ERR_UNSUPPORTED: a product the tensor-core kernel does not take; compose the three
+            check(rc, "tile_glu")
+            return out.reshape(*indices.shape, down.output_dims)
 
     def product(lin, a):
         return tile_matmul(lin.blocks, lin.kind, (lin.num_experts, lin.output_dims, lin.input_dims), a, tiles)

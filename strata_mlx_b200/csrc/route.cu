@@ -53,6 +53,23 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
     out[i] = from_f32<T>(swiglu_mlx<T>(to_f32(g[i]), to_f32(u[i])));
 }
 
+// 16 bytes a thread (8 values of a 2-byte type; n8 = n / 8, every pointer 16-byte aligned)
+template <typename T>
+__global__ void swiglu16_kernel(const uint4* __restrict__ g, const uint4* __restrict__ u, int64_t n8,
+                                uint4* __restrict__ out) {
+  static_assert(sizeof(T) == 2, "16-byte vectors of a 2-byte type");
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint4 gv = g[i], uv = u[i];
+    const T* gs = reinterpret_cast<const T*>(&gv);
+    const T* us = reinterpret_cast<const T*>(&uv);
+    uint4 o;
+    T* os = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) os[j] = from_f32<T>(swiglu_mlx<T>(to_f32(gs[j]), to_f32(us[j])));
+    out[i] = o;
+  }
+}
+
 }  // namespace sc
 
 using namespace sc;
@@ -123,7 +140,18 @@ extern "C" int sc_swiglu(const void* gate, const void* up, int64_t n, int dtype,
   if (n == 0) return SC_OK;
   const int threads = 256;
   const int grid = int(std::min<int64_t>(ceil_div(n, threads), 148 * 8));
+  const bool vec = dtype != SC_F32 && n % 8 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) |
+                     reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   bool ok = dispatch_dtype(dtype, [&]<typename T>() {
+    if constexpr (sizeof(T) == 2) {
+      if (vec) {
+        const int g8 = int(std::min<int64_t>(ceil_div(n / 8, threads), 148 * 8));
+        swiglu16_kernel<T><<<g8, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const uint4*>(gate), static_cast<const uint4*>(up), n / 8, static_cast<uint4*>(out));
+        return;
+      }
+    }
     swiglu_kernel<T><<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const T*>(gate),
                                                                                static_cast<const T*>(up), n,
                                                                                static_cast<T*>(out));

@@ -285,13 +285,13 @@ __device__ __forceinline__ void tmem_st32_async(uint32_t taddr, const uint32_t (
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-template <int KIND, typename T>
+template <int KIND, typename T, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     tile_mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap16,
                     const __grid_constant__ CUtensorMap amap32, const __grid_constant__ CUtensorMap amap64,
                     const __grid_constant__ CUtensorMap amap128, const uint8_t* __restrict__ blocks, int experts,
                     int rows, int cols, int64_t rbytes, int phases, int P, const uint32_t* __restrict__ tile_expert,
-                    float* __restrict__ c, int* err, int raw_stages) {
+                    const TileOut to, int* err, int raw_stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Layout L = layout(KIND, raw_stages);
@@ -624,14 +624,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0 && quarter == 0) TT(6, ic);
       tc_fence_after();
       const int row = r0 + 32 * quarter + lane;
-      float* out = c + int64_t(st) * TOKENS_TILE * rows + row;
       for (int n0 = 0; n0 < nt * TOKENS_TILE; n0 += 32) {
         float v[32];
         tmem_ld32(tmem + (uint32_t(32 * quarter) << 16) + uint32_t(ACC_COL + b * NMAX + n0), v);
         const int n = min(32, nt * TOKENS_TILE - n0);
+        const int64_t at = (int64_t(st) * TOKENS_TILE + n0) * rows + row;  // slot st 16 + n0 (+ i), row
+        if constexpr (MODE == 0) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (i < n) out[int64_t(n0 + i) * rows] = v[i];
+          for (int i = 0; i < 32; ++i)
+            if (i < n) to.c[at + int64_t(i) * rows] = v[i];
+        } else if constexpr (MODE == 1) {
+          T* o = static_cast<T*>(to.out) + at;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < n) o[int64_t(i) * rows] = from_f32<T>(v[i]);
+        } else {
+          // lane j holds the pair of slot st 16 + n0 + j; the pairs go to every lane by shuffles
+          const int mine = lane < n ? to.pair_of_slot[st * TOKENS_TILE + n0 + lane] : -1;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int p = __shfl_sync(0xffffffffu, mine, i);
+            if (p >= 0) static_cast<T*>(to.out)[int64_t(p) * rows + row] = from_f32<T>(v[i]);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -689,7 +704,7 @@ inline int phases_of(int64_t rb) {
 
 template <int KIND, typename T>
 int launch(const uint8_t* blocks, int experts, int rows, int cols, int64_t rb, const void* a, int P,
-           const uint32_t* tile_expert, float* c, int* err, cudaStream_t s) {
+           const uint32_t* tile_expert, const TileOut& to, int* err, cudaStream_t s) {
   EncodeTiled enc = encode_tiled();
   if (!enc) return SC_ERR_CUDA;
   const cuuint32_t estr[2] = {1, 1};
@@ -719,19 +734,21 @@ int launch(const uint8_t* blocks, int experts, int rows, int cols, int64_t rb, c
   constexpr int RS = raw_stages_for(KIND);
   constexpr int smem = layout(KIND, RS).total;
   static_assert(smem <= SMEM_LIMIT, "tile_mma shared memory");
-  auto kern = tile_mma_kernel<KIND, T>;
-  static bool set[64] = {};
+  auto kern = to.mode == 0 ? tile_mma_kernel<KIND, T, 0>
+            : to.mode == 1 ? tile_mma_kernel<KIND, T, 1>
+                           : tile_mma_kernel<KIND, T, 2>;
+  static bool set[3][64] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return SC_ERR_CUDA;
-  if (!set[dev]) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || to.mode < 0 || to.mode > 2) return SC_ERR_CUDA;
+  if (!set[to.mode][dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return SC_ERR_CUDA;
-    set[dev] = true;
+    set[to.mode][dev] = true;
   }
   const int grid = sm_count();
   if (grid <= 0) return SC_ERR_CUDA;
   kern<<<grid, THREADS, smem, s>>>(wmap, amaps[0], amaps[1], amaps[2], amaps[3], blocks, experts, rows, cols, rb,
-                                   phases, P, tile_expert, c, err, RS);
+                                   phases, P, tile_expert, to, err, RS);
   return cudaGetLastError() == cudaSuccess ? SC_OK : SC_ERR_CUDA;
 }
 
@@ -761,14 +778,14 @@ bool tile_mma_takes(int kind, int experts, int rows, int cols, int a_dtype, int 
 }
 
 int tile_mma_launch(int kind, const uint8_t* blocks, int experts, int rows, int cols, int64_t rbytes, const void* a,
-                    int a_dtype, int P, const uint32_t* tile_expert, float* c, int* err, cudaStream_t s) {
+                    int a_dtype, int P, const uint32_t* tile_expert, const TileOut& to, int* err, cudaStream_t s) {
   if (!tile_mma_takes(kind, experts, rows, cols, a_dtype, P, a, blocks)) return SC_ERR_UNSUPPORTED;
   int rc = SC_ERR_UNSUPPORTED;
   dispatch_kind(kind, [&]<int KIND>() {
     if (a_dtype == SC_BF16)
-      rc = tm::launch<KIND, __nv_bfloat16>(blocks, experts, rows, cols, rbytes, a, P, tile_expert, c, err, s);
+      rc = tm::launch<KIND, __nv_bfloat16>(blocks, experts, rows, cols, rbytes, a, P, tile_expert, to, err, s);
     else
-      rc = tm::launch<KIND, __half>(blocks, experts, rows, cols, rbytes, a, P, tile_expert, c, err, s);
+      rc = tm::launch<KIND, __half>(blocks, experts, rows, cols, rbytes, a, P, tile_expert, to, err, s);
   });
   return rc;
 }

@@ -166,8 +166,11 @@ extern "C" int sc_tile_matmul(int kind, const void* blocks, int experts, int row
   const int64_t rb = row_bytes(kind, cols);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a_dtype != SC_F32) {
+    TileOut to{};
+    to.mode = 0;
+    to.c = c;
     const int rc = tile_mma_launch(kind, static_cast<const uint8_t*>(blocks), experts, rows, cols, rb, a, a_dtype, P,
-                                   tile_expert, c, err, s);
+                                   tile_expert, to, err, s);
     if (rc != SC_ERR_UNSUPPORTED) return rc;
   }
   int rc = SC_ERR_DTYPE;
@@ -177,4 +180,61 @@ extern "C" int sc_tile_matmul(int kind, const void* blocks, int experts, int row
     });
   });
   return rc;
+}
+
+// ---- a prompt's three tile products in one call (blocks.py:566-576 _tiled_glu): gate and up in A's type, their
+// swiglu (sc_swiglu, mlx-lm's rounding), down written in the pairs' order; the same bits as the three tile_matmul
+// calls, the swiglu and the unsort
+
+__global__ void slot_pairs_kernel(const uint32_t* __restrict__ where, int pairs, int P, int* __restrict__ pos) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p < pairs && where[p] < uint32_t(P)) pos[where[p]] = p;
+}
+
+static size_t glu_part(int P, int inter) { return (size_t(P) * inter * 2 + 15) / 16 * 16; }
+
+extern "C" size_t sc_tile_glu_workspace(int P, int inter, int a_dtype) {
+  if (P < 0 || inter < 1 || (a_dtype != SC_F16 && a_dtype != SC_BF16)) return 0;
+  return 3 * glu_part(P, inter) + (size_t(P) * 4 + 15) / 16 * 16;
+}
+
+extern "C" int sc_tile_glu(int kind_gate, const void* gate, int kind_up, const void* up, int kind_down, const void* down,
+                           int experts, int hidden, int inter, const void* a, int a_dtype, int P,
+                           const uint32_t* tile_expert, const uint32_t* where, int pairs, void* out, void* workspace,
+                           size_t workspace_bytes, int* err, void* stream) {
+  if (!gate || !up || !down || !a || !tile_expert || !where || !out || experts < 1 || P < 0 || pairs < 0)
+    return SC_ERR_ARG;
+  if (a_dtype != SC_F16 && a_dtype != SC_BF16) return SC_ERR_UNSUPPORTED;
+  if (P % TOKENS_TILE) return SC_ERR_SHAPE;
+  if (!workspace || workspace_bytes < sc_tile_glu_workspace(P, inter, a_dtype)) return SC_ERR_WORKSPACE;
+  if (!tile_mma_takes(kind_gate, experts, inter, hidden, a_dtype, P, a, gate) ||
+      !tile_mma_takes(kind_up, experts, inter, hidden, a_dtype, P, a, up) ||
+      !tile_mma_takes(kind_down, experts, hidden, inter, a_dtype, P, workspace, down))
+    return SC_ERR_UNSUPPORTED;
+  if (P == 0) return SC_OK;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* h = ws;                               // (P, inter): swiglu, the down product's A
+  void* g = ws + glu_part(P, inter);          // (P, inter): the gate product in A's type
+  void* u = ws + 2 * glu_part(P, inter);      // (P, inter): the up product
+  int* pos = reinterpret_cast<int*>(ws + 3 * glu_part(P, inter));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(pos, 0xFF, size_t(P) * 4, s) != cudaSuccess) return SC_ERR_CUDA;
+  if (pairs > 0) slot_pairs_kernel<<<int(ceil_div(pairs, 256)), 256, 0, s>>>(where, pairs, P, pos);
+  if (cudaGetLastError() != cudaSuccess) return SC_ERR_CUDA;
+  TileOut to{};
+  to.mode = 1;
+  to.out = g;
+  if (int rc = tile_mma_launch(kind_gate, static_cast<const uint8_t*>(gate), experts, inter, hidden,
+                               row_bytes(kind_gate, hidden), a, a_dtype, P, tile_expert, to, err, s))
+    return rc;
+  to.out = u;
+  if (int rc = tile_mma_launch(kind_up, static_cast<const uint8_t*>(up), experts, inter, hidden,
+                               row_bytes(kind_up, hidden), a, a_dtype, P, tile_expert, to, err, s))
+    return rc;
+  if (int rc = sc_swiglu(g, u, int64_t(P) * inter, a_dtype, h, stream)) return rc;
+  to.mode = 2;
+  to.out = out;
+  to.pair_of_slot = pos;
+  return tile_mma_launch(kind_down, static_cast<const uint8_t*>(down), experts, hidden, inter,
+                         row_bytes(kind_down, inter), h, a_dtype, P, tile_expert, to, err, s);
 }

@@ -16,8 +16,18 @@ inline bool tileable(int kind, int rows, int cols) {
 // The tcgen05 tile product (tile_mma.cu) for float16 / bfloat16 activations; SC_ERR_UNSUPPORTED where it
 // does not take the call (tile_mma_takes false: the caller then runs the CUDA-core kernel). Bounded waits that give up record
 // SC_ERR_TIMEOUT in *err (when err is not null).
+// What the tile product's epilogue writes: 0 C float32 (P, rows); 1 C in A's type (P, rows); 2 C in A's type at row
+// pair_of_slot[slot] of `out` (pairs, rows), nothing for slots of no pair. (A swiglu of the gate product in the up
+// product's epilogue measured 2.4x slower than the plain epilogue: it runs as its own pass.)
+struct TileOut {
+  int mode;
+  float* c;
+  void* out;
+  const int* pair_of_slot;
+};
+
 bool tile_mma_takes(int kind, int experts, int rows, int cols, int a_dtype, int P, const void* a, const void* blocks);
 int tile_mma_launch(int kind, const uint8_t* blocks, int experts, int rows, int cols, int64_t rbytes, const void* a,
-                    int a_dtype, int P, const uint32_t* tile_expert, float* c, int* err, cudaStream_t s);
+                    int a_dtype, int P, const uint32_t* tile_expert, const TileOut& o, int* err, cudaStream_t s);
 
 }  // namespace sc

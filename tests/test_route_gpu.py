@@ -111,3 +111,25 @@ def test_the_decode_block_is_the_oracles(cuda, monkeypatch, kinds, tokens):
     got2 = routed(x).float().cpu().numpy()
     assert np.abs(got2 - want).max() <= 2e-2 * np.abs(want).max()
     np.testing.assert_array_equal(got2, got)  # the Python block and the C chain give the same bits
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_swiglu_16_byte_and_scalar_paths_match_the_oracle(cuda, dt):
+    """B.swiglu (sc_swiglu): the 16-byte path (aligned, n a multiple of 8) and the scalar one (an odd offset) give
+    the same bits, and the oracle's swiglu (blocks.py:230-238) within a unit of the type (numpy's exp and CUDA's
+    expf round apart now and then)."""
+    torch.manual_seed(5)
+    n = 8 * 12345
+    g = (torch.randn(n + 1) * 4).to(dt).cuda()
+    u = (torch.randn(n + 1) * 2).to(dt).cuda()
+    vec = B.swiglu(g[:n], u[:n])
+    odd = B.swiglu(g[1:], u[1:])
+    assert torch.equal(B.swiglu(g[1 : n + 1].clone(), u[1 : n + 1].clone()), odd)
+    assert torch.equal(vec[1:], B.swiglu(g[1:n].clone(), u[1:n].clone()))
+    nd = "bfloat16" if dt == torch.bfloat16 else "float16"
+    want = R.swiglu(g[:n].float().cpu().numpy(), u[:n].float().cpu().numpy(), nd)
+    got = vec.float().cpu().numpy()
+    same = got == want
+    assert same.mean() > 0.99, same.mean()
+    unit = np.abs(want) * (2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10) + 1e-30
+    assert (np.abs(got - want) <= unit)[~same].all()

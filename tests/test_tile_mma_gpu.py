@@ -87,3 +87,28 @@ def test_a_call_with_no_expert_tiles_writes_nothing(cuda):
     torch.cuda.synchronize()
     _lib.check_device_errors()
     assert bool((out == 7.0).all())
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_the_one_call_prompt_is_the_three_products(cuda, monkeypatch, dt):
+    """_tiled_glu through sc_tile_glu (swiglu and the unsort in the epilogues) gives the bits of the composition of
+    tile_matmul, swiglu and index_select (blocks.py:566-576)."""
+    rng = np.random.default_rng(9)
+    experts, hidden, inner, k, tokens = 12, 512, 256, 4, 300
+    lins = {}
+    for name, kind, (rows, cols) in (("gate", "IQ3_XXS", (inner, hidden)), ("up", "IQ3_XXS", (inner, hidden)),
+                                     ("down", "IQ3_S", (hidden, inner))):
+        data = blocks_numpy(kind, experts, rows, cols, rng, uniform=0.002)
+        lins[name] = B.BlockSwitchLinear(dev(data), kind, (experts, rows, cols))
+    x = dev(rng.standard_normal((1, tokens, hidden)).astype(np.float32)).to(dt)
+    idx = dev(rng.integers(0, experts, (1, tokens, k)).astype(np.int32))
+    one = B._tiled_glu(x, idx, lins["up"], lins["gate"], lins["down"])
+    # the composition: tile_matmul x 3, swiglu, the unsort
+    tiles, token, where = B.tiles_of(idx, experts)
+    a = x.reshape(-1, hidden).index_select(0, token.to(torch.int64))
+    prod = lambda lin, a: B.tile_matmul(lin.blocks, lin.kind, (experts, lin.output_dims, lin.input_dims), a, tiles)
+    h = B.swiglu(prod(lins["gate"], a).to(dt), prod(lins["up"], a).to(dt))
+    want = prod(lins["down"], h).index_select(0, where.to(torch.int64)).to(dt).reshape(1, tokens, k, hidden)
+    torch.cuda.synchronize()
+    _lib.check_device_errors()
+    assert one.shape == want.shape and torch.equal(one, want)
