@@ -44,6 +44,14 @@ __device__ unsigned long long g_trace[3][8192][8];
       if (blockIdx.x < 8192) g_trace[k][blockIdx.x][p] = t_;                 \
     }                                                                        \
   } while (0)
+#define TRACE_SMID(k, p)                                                     \
+  do {                                                                       \
+    if (threadIdx.x == 0) {                                                  \
+      unsigned int s_;                                                       \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(s_));                         \
+      if (blockIdx.x < 8192) g_trace[k][blockIdx.x][p] = s_ + 1;             \
+    }                                                                        \
+  } while (0)
 #define TRACE_WARP(k, p)                                                     \
   do {                                                                       \
     if ((threadIdx.x & 31) == 0) {                                           \
@@ -55,6 +63,9 @@ __device__ unsigned long long g_trace[3][8192][8];
 #else
 #define TRACE_POINT(k, p) \
   do {                    \
+  } while (0)
+#define TRACE_SMID(k, p) \
+  do {                   \
   } while (0)
 #define TRACE_WARP(k, p) \
   do {                   \
@@ -159,8 +170,6 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
     }
     __syncthreads();
   }
-  // only now may the gate/up kernel start: it reads the activations before it waits on this kernel
-  pdl_launch_dependents();
   if (wrow) {
     for (int t = 0; t < T_; ++t) {
       const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const T*>(L.x) + int64_t(t) * H);
@@ -183,6 +192,10 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   if (tid == 0) s_last = atomic_add_acq_rel(L.ticket, 1) == int(gridDim.x) - 1;  // release this block's logits
   __syncthreads();
   if (!s_last) return;
+  // only now may the gate/up kernel start (it reads the activations before it waits on this kernel), when the other
+  // blocks of this kernel are leaving: launched while they held their SMs, its blocks went to the other SMs only
+  // (these blocks' registers leave room for none), a quarter of the SMs without one
+  pdl_launch_dependents();
   TRACE_POINT(0, 3);
 
   // ---- the last block: top-k of each token. Every step is a few dependent operations across all lanes: a long
@@ -396,6 +409,7 @@ __host__ __device__ inline GuSmem gu_smem(int tokens, int H, int64_t rb) {
 template <int KIND, typename T>
 __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   TRACE_POINT(1, 0);
+  TRACE_SMID(1, 2);
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T_ = L.T, H = L.H;
@@ -541,6 +555,7 @@ __host__ __device__ inline DnSmem dn_smem(int tokens, int K, int stage_bytes, in
 template <int KIND, typename T>
 __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   TRACE_POINT(2, 0);
+  TRACE_SMID(2, 6);  // (slots 6 and 7 stamp the peer-memory epilogue; a single-device trace uses 6 for the SM)
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T_ = L.T, K = L.K, H = L.H;
@@ -741,7 +756,9 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
   L.dn_stage = align16(RC * int(std::max(L.rb_d, L.rb_sd))) + align16(L.T * L.hstride * 2);
   L.dn_stages = std::max(2, std::min({MAX_STAGES, max_units, (144 * 1024) / L.dn_stage}));
   if (L.dn_stages > DN_WARPS) L.dn_stages -= L.dn_stages % DN_WARPS;  // every warp the same number of stages
-  const int dn_total = dn_smem(L.T, L.K, L.dn_stage, L.dn_stages).total;
+  // one down block an SM: two on one SM (where the gate/up blocks left room first) ran twice as long, and the
+  // layer waits for the slowest; more than half an SM's shared memory keeps a second one off
+  const int dn_total = std::max(dn_smem(L.T, L.K, L.dn_stage, L.dn_stages).total, 116 * 1024);
   if (gu_total > 227 * 1024 || dn_total > 227 * 1024) return SC_ERR_SHAPE;
 
   auto kr = route_kernel<T>;
