@@ -141,7 +141,8 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
   return old;
 }
 
-template <typename T>
+// MT: the tokens the last block's registers are laid out for (1 for a one-token window: a shorter tail)
+template <typename T, int MT>
 __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   TRACE_POINT(0, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
@@ -219,15 +220,15 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   const int live = int(ceil_div(E, seg));  // warps with logits
   const int base = seg * warp;
   const bool ok0 = warp < live && base + lane < E, ok1 = warp < live && seg == 64 && base + 32 + lane < E;
-  uint32_t k0[MAXT], k1[MAXT];  // keys of invalid slots are 0, below every non-NaN logit's key
+  uint32_t k0[MT], k1[MT];  // keys of invalid slots are 0, below every non-NaN logit's key
 #pragma unroll
-  for (int t = 0; t < MAXT; ++t) {
+  for (int t = 0; t < MT; ++t) {
     k0[t] = ok0 && t < T_ ? fkey(__ldcg(L.logits + int64_t(t) * E + base + lane)) : 0u;
     k1[t] = ok1 && t < T_ ? fkey(__ldcg(L.logits + int64_t(t) * E + base + 32 + lane)) : 0u;
   }
   TRACE_WARP(0, 0);
 #pragma unroll
-  for (int t = 0; t < MAXT; ++t) {
+  for (int t = 0; t < MT; ++t) {
     const uint32_t mx = __reduce_max_sync(0xffffffffu, max(k0[t], k1[t]));
     if (lane == 0 && t < T_) w_max[t][warp] = mx;
   }
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
 #pragma unroll
     for (int j = 0; j < RT_WARPS; ++j) {
       const uint32_t a = j < live ? w_max[t][j] : 0u;
-      r += a > v || (a == v && j < lane);
+      r += int(a > v) | (int(a == v) & int(j < lane));
     }
     const uint32_t th = __reduce_max_sync(0xffffffffu, lane < live && r == K - 1 ? v : 0u);
     if (lane == 0) s_theta[t] = th;
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   __syncthreads();
   TRACE_WARP(0, 1);
 #pragma unroll
-  for (int t = 0; t < MAXT; ++t) {  // C
+  for (int t = 0; t < MT; ++t) {  // C
     if (t >= T_) break;
     const uint32_t th = s_theta[t];
     const bool in0 = ok0 && k0[t] >= th, in1 = ok1 && k1[t] >= th;
@@ -287,15 +288,27 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
         const bool in = lane + 32 * q < m;
         const uint32_t kc = in ? m_k[t][lane + 32 * q] : 0u, ic = in ? m_i[t][lane + 32 * q] : NONE;
         TRACE_WARP(0, 3);
+#ifdef SC_TRACE
+        const long long c0_ = clock64();
+#endif
         int r4[4] = {0, 0, 0, 0};
         for (int j = 0; j < m; j += 4) {  // entries past m hold stale values: masked by j + e < m
           const uint4 a = *reinterpret_cast<const uint4*>(&m_k[t][j]);
           const uint4 ai = *reinterpret_cast<const uint4*>(&m_i[t][j]);
           const uint32_t av[4] = {a.x, a.y, a.z, a.w}, aiv[4] = {ai.x, ai.y, ai.z, ai.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) r4[e] += j + e < m && (av[e] > kc || (av[e] == kc && aiv[e] < ic));
+          for (int e = 0; e < 4; ++e)  // bitwise, not && / ||: no branches in the chain
+            r4[e] += int(j + e < m) & (int(av[e] > kc) | (int(av[e] == kc) & int(aiv[e] < ic)));
         }
         const int r = r4[0] + r4[1] + r4[2] + r4[3];
+#ifdef SC_TRACE
+        const long long c1_ = clock64();
+        if (lane == 0) {
+          g_trace[0][4300 + t][0] = (unsigned long long)(c1_ - c0_);
+          g_trace[0][4300 + t][1] = (unsigned long long)m;
+          g_trace[0][4300 + t][2] = (unsigned long long)r;
+        }
+#endif
         if (in && r < K) {
           s_key[t * K + r] = kc;
           s_idx[t * K + r] = ic;
@@ -761,7 +774,7 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
   const int dn_total = std::max(dn_smem(L.T, L.K, L.dn_stage, L.dn_stages).total, 116 * 1024);
   if (gu_total > 227 * 1024 || dn_total > 227 * 1024) return SC_ERR_SHAPE;
 
-  auto kr = route_kernel<T>;
+  auto kr = L.T == 1 ? route_kernel<T, 1> : route_kernel<T, MAXT>;
   auto kg = gate_up_kernel<KGU, T>;
   auto kd = down_kernel<KD, T>;
   // the dynamic shared memory a launch may take is raised to what it needs (the opt-in limit counts the kernel's

@@ -115,12 +115,18 @@ __device__ __forceinline__ void warp_topk(const float* __restrict__ logits, int 
 // before the final rounding to T. y_k is at y[k * YSTRIDE].
 template <typename T, int YSTRIDE = 1>
 __device__ __forceinline__ float combine_one(const float* y, const float* w, int k, float g, float s) {
-  float acc = 0.f;
-  for (int j = 0; j < 8 && j < k; ++j) {
-    float part = 0.f;
-    for (int q = j; q < k; q += 8) part = __fadd_rn(__fmul_rn(y[q * YSTRIDE], w[q]), part);
-    acc = j == 0 ? part : __fadd_rn(part, acc);
-  }
+  // unrolled to the largest k with the products guarded: the same adds in the same order, without the loops'
+  // branches (a one-thread chain, on the decode block's critical path)
+  float part[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[j] = 0.f;
+#pragma unroll
+  for (int q = 0; q < TOPK_MAX_K; ++q)
+    if (q < k) part[q & 7] = __fadd_rn(__fmul_rn(y[q * YSTRIDE], w[q]), part[q & 7]);
+  float acc = part[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j)
+    if (j < k) acc = __fadd_rn(part[j], acc);
   const float routed = round_to<T>(acc);
   const float gate = round_to<T>(1.0f / (1.0f + expf(-g)));
   const float shared = round_to<T>(__fmul_rn(gate, s));

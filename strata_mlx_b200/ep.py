@@ -182,22 +182,31 @@ class EPDecodeChain:
         for l in layers:
             l.base.workspace(self.T, device)
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, refeed: int = 0) -> torch.Tensor:
+        """refeed: every `refeed` layers (an even number dividing the chain) the layer takes this rank's tokens x
+        again, not the previous layer's outputs -- for a synthetic chain, which has none of the norms a model puts
+        between its MoE blocks and would otherwise grow without bound."""
         lib = _lib.lib()
         xs = x.reshape(self.t, self.hidden)
         if xs.dtype != self.dtype:
             raise ValueError(f"activations of {xs.dtype}; the chain was built for {self.dtype}")
         xs = xs if xs.is_contiguous() else xs.contiguous()
+        seg = refeed or len(self.layers)
+        if seg % 2 or len(self.layers) % seg:
+            raise ValueError(f"refeed {refeed}: an even number that divides the {len(self.layers)} layers")
         d = ctypes.byref(self.ex.desc)
-        check(lib.sc_ep_feed(self.layers[0].base.layer_ref(), d, ptr(xs), stream()), "sc_ep_feed")
-        last = len(self.layers) - 1
-        for i, l in enumerate(self.layers):
-            ws = l.base.workspace(self.T, self.device)
-            ref = l.base.layer_ref()
-            check(lib.sc_moe_decode_layer_ep_p2p(ref, d, l.e0, l.e1, i % 2, ptr(ws), ws.numel(), stream()),
-                  "sc_moe_decode_layer_ep_p2p")
-            check(lib.sc_ep_combine(ref, d, i % 2, int(i == last), ptr(self.out), ptr(ws), ws.numel(), stream()),
-                  "sc_ep_combine")
+        for s0 in range(0, len(self.layers), seg):
+            # the segment's first window: this rank's tokens into every rank's window 0 (as a new call would)
+            check(lib.sc_ep_feed(self.layers[s0].base.layer_ref(), d, ptr(xs), stream()), "sc_ep_feed")
+            for i in range(s0, s0 + seg):
+                l = self.layers[i]
+                ws = l.base.workspace(self.T, self.device)
+                ref = l.base.layer_ref()
+                check(lib.sc_moe_decode_layer_ep_p2p(ref, d, l.e0, l.e1, i % 2, ptr(ws), ws.numel(), stream()),
+                      "sc_moe_decode_layer_ep_p2p")
+                last = int(i == s0 + seg - 1)
+                check(lib.sc_ep_combine(ref, d, i % 2, last, ptr(self.out), ptr(ws), ws.numel(), stream()),
+                      "sc_ep_combine")
         return self.out.reshape(x.shape)
 
     def check_errors(self) -> None:

@@ -75,6 +75,24 @@ def main():
                 print(f"rank {rank} peer chain t={t} step {step}: differs (max {diff})", flush=True)
         dist.barrier()
         chain.close()
+    # four layers fed again after two (refeed 2): the result is the last two layers on x, not all four in a row
+    for t in (1, 2):
+        chain = EP.EPDecodeChain([chain_par[0], chain_par[1], chain_par[1], chain_par[0]], t, dev)
+        for step in range(2):
+            x = torch.randn((t, H), generator=torch.Generator(device=dev).manual_seed(1000 + 100 * step + 10 * rank + t),
+                            device=dev).to(torch.bfloat16)
+            got = chain(x, refeed=2).clone()
+            want = x
+            for one in (chain_one[1], chain_one[0]):
+                want = torch.cat([one(want[i : i + 1]) for i in range(t)])
+            torch.cuda.synchronize()
+            chain.check_errors()
+            if not torch.equal(got, want):
+                bad += 1
+                diff = (got.float() - want.float()).abs().max().item()
+                print(f"rank {rank} refed chain t={t} step {step}: differs (max {diff})", flush=True)
+        dist.barrier()
+        chain.close()
     flag = torch.tensor([bad], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
