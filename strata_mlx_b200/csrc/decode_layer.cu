@@ -565,6 +565,53 @@ __host__ __device__ inline DnSmem dn_smem(int tokens, int K, int stage_bytes, in
   return s;
 }
 
+// Runs [n0, n1) of a unit's 16 down rows (in the stage `st`) times its h: the h columns of those runs first, from L2
+// into the stage (every load in flight at once; a bulk copy issued after the wait took ~1.3 us to land, these ~0.6),
+// then the products. acc: the C fragment (rows g, g + 8; tokens 2t, 2t + 1).
+template <int KIND, typename T>
+__device__ __forceinline__ void down_piece(const LayerDev& L, uint8_t* st, int hoff, int u, int n0, int n1, bool shared,
+                                           uint32_t mask, const uint32_t* grid, int lane, float (&acc)[4]) {
+  const int T_ = L.T, g = lane >> 2, t = lane & 3;
+  T* hs = reinterpret_cast<T*>(st + hoff);
+  {
+    const T* hu = static_cast<const T*>(L.h) + int64_t(u) * T_ * L.hstride;
+    const int per = 4 * (n1 - n0), n16 = T_ * per;  // 16-byte pieces a token, in all
+    constexpr int PER = 2;  // a one-token unit's h is 64 pieces: two a lane (more only cost registers)
+    for (int i0 = 0; i0 < n16; i0 += 32 * PER) {
+      uint4 v[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int i = i0 + 32 * j + lane;
+        if (i < n16) v[j] = __ldcg(reinterpret_cast<const uint4*>(hu + (i / per) * L.hstride + 32 * n0 + 8 * (i % per)));
+      }
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int i = i0 + 32 * j + lane;
+        if (i < n16) *reinterpret_cast<uint4*>(hs + (i / per) * L.hstride + 32 * n0 + 8 * (i % per)) = v[j];
+      }
+    }
+    __syncwarp();
+  }
+  const int64_t rb = shared ? L.rb_sd : L.rb_d;
+  const bool mine = g < T_ && ((mask >> g) & 1u);
+  const uint8_t* ra = st + g * rb;
+  const uint8_t* rbp = st + (g + 8) * rb;
+  acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll 4
+  for (int n = n0; n < n1; ++n) {
+    uint4 xv = make_uint4(0, 0, 0, 0);
+    if (mine) xv = *reinterpret_cast<const uint4*>(hs + g * L.hstride + 32 * n + 8 * t);
+    uint32_t pa[4], pb[4];
+    const float sa = dec8<KIND, T>(ra, n, t, grid, pa), sb = dec8<KIND, T>(rbp, n, t, grid, pb);
+    const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816<T>(d, a0, xv.x, xv.y);
+    mma16816<T>(d, a1, xv.z, xv.w);
+    acc[0] = fmaf(sa, d[0], acc[0]); acc[1] = fmaf(sa, d[1], acc[1]);
+    acc[2] = fmaf(sb, d[2], acc[2]); acc[3] = fmaf(sb, d[3], acc[3]);
+  }
+}
+
 template <int KIND, typename T>
 __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   TRACE_POINT(2, 0);
@@ -580,8 +627,6 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   float* ys = reinterpret_cast<float*>(smem + S.ys);    // (T, K + 1, 16): routed outputs, then the shared one
   uint8_t* stage0 = smem + S.stages;
   const int r0 = blockIdx.x * RC;
-  const int hbytes = T_ * L.hstride * 2;  // a unit's h: its tokens' rows
-  const int hoff = align16(RC * int(max(L.rb_d, L.rb_sd)));
   pdl_launch_dependents();  // the next layer's router may load its weights now
 
   if (tid == 0) {
@@ -602,7 +647,10 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   __syncthreads();
   TRACE_POINT(2, 1);
   const int units = plan->units;
-  // the down rows of the first units do not wait for the gate/up kernel; their h does
+  // the down rows of the first units do not wait for the gate/up kernel; their h does, and the consumer warp copies
+  // it into the stage itself (a bulk copy issued by the producer after the wait took ~1.3 us to land, the warp's
+  // loads ~0.6; loads of h inside the product's loop serialised it)
+  const int hoff = align16(RC * int(max(L.rb_d, L.rb_sd)));
   auto weights = [&](int u, int s) {
     uint8_t* dst = stage0 + s * L.dn_stage;
     if (u == 0) {
@@ -614,84 +662,60 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   auto weight_bytes = [&](int u) -> uint32_t { return u == 0 ? uint32_t(L.Is > 0 ? RC * L.rb_sd : 0) : uint32_t(RC * L.rb_d); };
   if (warp == DN_WARPS && lane == 0) {
     for (int u = 0; u < min(units, L.dn_stages); ++u) {
-      mbar_expect_tx(&full[u], weight_bytes(u));
+      if (weight_bytes(u) == 0) {  // no shared expert: nothing to load for unit 0
+        mbar_arrive(&full[u]);
+        continue;
+      }
+      mbar_arrive_expect_tx(&full[u], weight_bytes(u));
       weights(u, u);
     }
   }
   pdl_wait();  // h
   TRACE_POINT(2, 2);
 
-  if (warp == DN_WARPS) {  // ---- producer: h of the first units, then the ring's later units whole
+  if (warp == DN_WARPS) {  // ---- producer: the ring's later units (unit 0, the shared expert, is never one)
     if (lane == 0) {
-      for (int u = 0; u < units; ++u) {
+      for (int u = L.dn_stages; u < units; ++u) {
         const int s = u % L.dn_stages;
-        uint8_t* dst = stage0 + s * L.dn_stage;
-        const bool none = u == 0 && L.Is == 0;
-        if (u >= L.dn_stages) {
-          if (!mbar_wait(&empty[s], ((u / L.dn_stages) - 1) & 1, L.err)) break;
-          if (none) {
-            mbar_arrive(&full[s]);
-            continue;
-          }
-          mbar_arrive_expect_tx(&full[s], weight_bytes(u) + uint32_t(hbytes));
-          weights(u, s);
-        } else {
-          if (none) {
-            mbar_arrive(&full[s]);
-            continue;
-          }
-          mbar_arrive_expect_tx(&full[s], uint32_t(hbytes));
-        }
-        bulk_load(dst + hoff, static_cast<const T*>(L.h) + int64_t(u) * T_ * L.hstride, uint32_t(hbytes), &full[s]);
+        if (!mbar_wait(&empty[s], ((u / L.dn_stages) - 1) & 1, L.err)) break;
+        mbar_arrive_expect_tx(&full[s], weight_bytes(u));
+        weights(u, s);
       }
     }
     return;
   }
 
-  // ---- consumers: every use of a stage goes to the same warp, in order (unit u to warp (u % stages) % DN_WARPS), so
-  // that a warp waits on a stage's n-th phase only after it consumed the (n-1)-th: a wait on parity 1 while the
-  // barrier is still in its first phase would return at once
   const int g = lane >> 2, t = lane & 3;
-  for (int u = 0; u < units; ++u) {
-    const int s = u % L.dn_stages;
-    if (s % DN_WARPS != warp) continue;
-    if (!mbar_wait(&full[s], (u / L.dn_stages) & 1, L.err)) break;
-    const bool shared = u == 0;
-    if (shared && L.Is == 0) {
+  {
+    // ---- consumers, a ring: every use of a stage goes to the same warp, in order (unit u to warp (u % stages) %
+    // DN_WARPS), so that a warp waits on a stage's n-th phase only after it consumed the (n-1)-th: a wait on parity 1
+    // while the barrier is still in its first phase would return at once. The warp's units are walked directly (a
+    // scan of every unit took a runtime modulo per unit: ~1 us before the last warps reached their first unit).
+    // Stage count S <= DN_WARPS or a multiple of it; the warp owns stages w, w + DN_WARPS, ... < S; after unit u in
+    // stage s comes u + DN_WARPS while s + DN_WARPS < S, else stage w of the next round.
+    const int S_ = L.dn_stages;
+    for (int u = warp < S_ ? warp : units, s = warp; u < units;
+         u = s + DN_WARPS < S_ ? u + DN_WARPS : u - s + S_ + warp, s = u % S_) {
+      if (!mbar_wait(&full[s], (u / S_) & 1, L.err)) break;
+      const bool shared = u == 0;
+      if (shared && L.Is == 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        continue;
+      }
+      const uint32_t mask = plan->unit[u].tokmask, kpack = plan->unit[u].kpack;
+      float acc[4];
+      down_piece<KIND, T>(L, stage0 + s * L.dn_stage, hoff, u, 0, (shared ? L.Is : L.I) / 32, shared, mask, grid,
+                          lane, acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      continue;
-    }
-    const uint8_t* st = stage0 + s * L.dn_stage;
-    const T* hs = reinterpret_cast<const T*>(st + hoff);
-    const int runs = (shared ? L.Is : L.I) / 32;
-    const int64_t rb = shared ? L.rb_sd : L.rb_d;
-    const uint32_t mask = plan->unit[u].tokmask, kpack = plan->unit[u].kpack;
-    const bool mine = g < T_ && ((mask >> g) & 1u);
-    const uint8_t* ra = st + g * rb;
-    const uint8_t* rbp = st + (g + 8) * rb;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int n = 0; n < runs; ++n) {
-      uint4 xv = make_uint4(0, 0, 0, 0);
-      if (mine) xv = *reinterpret_cast<const uint4*>(hs + g * L.hstride + 32 * n + 8 * t);
-      uint32_t pa[4], pb[4];
-      const float sa = dec8<KIND, T>(ra, n, t, grid, pa), sb = dec8<KIND, T>(rbp, n, t, grid, pb);
-      const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816<T>(d, a0, xv.x, xv.y);
-      mma16816<T>(d, a1, xv.z, xv.w);
-      acc[0] = fmaf(sa, d[0], acc[0]); acc[1] = fmaf(sa, d[1], acc[1]);
-      acc[2] = fmaf(sb, d[2], acc[2]); acc[3] = fmaf(sb, d[3], acc[3]);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {  // C fragment: rows g, g + 8; tokens 2t, 2t + 1
-      const int m = (q < 2 ? 0 : 8) + g, tok = 2 * t + (q & 1);
-      if (tok < T_ && ((mask >> tok) & 1u)) {
-        const int k = shared ? K : int((kpack >> (4 * tok)) & 15u);
-        ys[(tok * (K + 1) + k) * RC + m] = round_to<T>(acc[q]);
+      for (int q = 0; q < 4; ++q) {  // C fragment: rows g, g + 8; tokens 2t, 2t + 1
+        const int m = (q < 2 ? 0 : 8) + g, tok = 2 * t + (q & 1);
+        if (tok < T_ && ((mask >> tok) & 1u)) {
+          const int k = shared ? K : int((kpack >> (4 * tok)) & 15u);
+          ys[(tok * (K + 1) + k) * RC + m] = round_to<T>(acc[q]);
+        }
       }
     }
   }
