@@ -482,6 +482,46 @@ def stage_bytes(kind: str) -> dict:
     }
 
 
+def window_stream(layers, device, tokens: int = 8, reps: int = 20) -> dict:
+    """The fused decode block over a window of `tokens` tokens (its largest; a decode batch of 8 sequences), the 48
+    layers replayed as a CUDA graph: each layer reads every distinct routed expert of the window once (~60-80 of
+    512), so a step streams a few GB. Algorithmic bytes: per layer the distinct experts' gate, up and down blocks
+    (counted from the routes the layers chose), the shared expert, the router. Shows the decode kernels' rate once
+    a layer carries enough bytes; one-token layers are latency-bound."""
+    from strata_mlx_b200 import fused as F
+
+    g = F.DecodeGraph(layers, tokens=tokens, device=device, capture=True)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(8)
+    xs = torch.randn((reps + 3, tokens, H), generator=gen, device=device).to(torch.bfloat16)
+    for i in range(3):
+        g.x.copy_(xs[i])
+        g.replay()
+    torch.cuda.synchronize()
+    s = g.stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nbytes = 0.0
+    total_us = 0.0
+    for i in range(reps):
+        with torch.cuda.stream(s):
+            g.x.copy_(xs[3 + i])
+            e0.record(s)
+            g.replay()
+            e1.record(s)
+        torch.cuda.synchronize()
+        total_us += e0.elapsed_time(e1) * 1e3
+        for l in layers:  # the routes this step chose: the distinct experts each layer read
+            used = int(torch.unique(l.routes(tokens, device)[0].view(torch.int32)).numel())
+            per_expert = 2 * I * row_bytes(l.kind, H) + H * row_bytes(l.kind, I)
+            shared = 2 * IS * row_bytes(l.kind, H) + H * row_bytes(l.kind, IS)
+            nbytes += used * per_expert + shared + E * H * 2
+    us = total_us / reps
+    nbytes /= reps
+    return {"api": "strata_mlx_b200.fused.DecodeGraph (48 layers, graph replay)", "tokens": tokens,
+            "bytes_per_step": nbytes, "us_per_step": us, "gbs": nbytes / (us * 1e-6) / 1e9,
+            "tok_per_s": tokens / (us * 1e-6)}
+
+
 def time_stages(layers, graph, device, reps: int, capture: bool) -> dict:
     """Each of the fused path's three kernels alone: one launch per layer on the workspace the last step left,
     48 launches (with their programmatic dependencies) replayed as a graph, timed with CUDA events on its stream."""
@@ -720,6 +760,11 @@ def main() -> None:
             "expert_matvec_gbs": achieved, "expert_matvec_frac_of_8tbs": achieved / 8000.0,
             "gpu_launches": 3 * args.layers * args.steps, "gpu_launches_per_step": 3 * args.layers, "clocks": clk}
     line["chain_gbs"] = (line["expert_bytes_per_step"] + sum(stage_bytes(l.kind)["route"] for l in layers)) / (ms * 1e-3) / 1e9
+    if world == 1:
+        st = window_stream(layers, device)
+        st["frac"] = st["gbs"] / pk["hbm_gbs"]
+        st["peak"] = pk["hbm_gbs"]
+        line["window8_stream"] = st
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cb = cpu_sample(args.kinds, 12.0, True)
         cpu_ms = step_seconds(cb["per_layer_s"], args.layers, args.kinds) * 1000.0
