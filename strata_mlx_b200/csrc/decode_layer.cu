@@ -141,7 +141,8 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
   return old;
 }
 
-// MT: the tokens the last block's registers are laid out for (1 for a one-token window: a shorter tail)
+// MT: the tokens the last block's registers are laid out for (1, 2, 4 or MAXT, the window's tokens or more: a shorter
+// tail for small windows, as expert parallel makes them: one token a rank)
 template <typename T, int MT>
 __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   TRACE_POINT(0, 0);
@@ -798,7 +799,10 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
   const int dn_total = std::max(dn_smem(L.T, L.K, L.dn_stage, L.dn_stages).total, 116 * 1024);
   if (gu_total > 227 * 1024 || dn_total > 227 * 1024) return SC_ERR_SHAPE;
 
-  auto kr = L.T == 1 ? route_kernel<T, 1> : route_kernel<T, MAXT>;
+  auto kr = L.T == 1   ? route_kernel<T, 1>
+            : L.T == 2 ? route_kernel<T, 2>
+            : L.T <= 4 ? route_kernel<T, 4>
+                       : route_kernel<T, MAXT>;
   auto kg = gate_up_kernel<KGU, T>;
   auto kd = down_kernel<KD, T>;
   // the dynamic shared memory a launch may take is raised to what it needs (the opt-in limit counts the kernel's

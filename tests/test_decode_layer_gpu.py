@@ -45,7 +45,7 @@ KINDS = [("Q2_0", "Q2_0", "Q2_0"), ("IQ3_S", "IQ3_S", "IQ3_S"), ("IQ3_XXS", "IQ3
 
 
 @pytest.mark.parametrize("kinds", KINDS)
-@pytest.mark.parametrize("tokens", [1, 2, 5, 8])
+@pytest.mark.parametrize("tokens", [1, 2, 3, 5, 8])
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 def test_the_three_kernel_block_is_the_oracles(cuda, kinds, tokens, dt):
     L, lin, shared, W, rng = build(kinds, tokens)
