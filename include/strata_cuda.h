@@ -160,6 +160,17 @@ SC_API int sc_tile_glu(int kind_gate, const void* gate, int kind_up, const void*
                        size_t workspace_bytes, int* err, void* stream);
 SC_API size_t sc_tile_glu_workspace(int P, int inter, int a_dtype);
 
+/* strata_mlx/dense.py:109-167 ScaledLinear: a dense layer held as Q6_K's three parts, a weight being
+ * code * scale * d: codes int8 (rows, cols), scales int8 (rows, cols / 16), d float16 (rows, cols / d_step).
+ * rows by 4 and cols by 256 (dense.py:97-99 fits), d_step a multiple of 16 dividing cols; codes and x 16-byte
+ * aligned. sc_scaled_matvec: out (tokens, rows) = x (tokens, cols) . W^T in x's type, float32 sums, tokens <= 8
+ * (dense.py:141-167, the window kernel). sc_scaled_floats: W (rows, cols) in out_dtype, each weight
+ * float(d) * float(scale) * float(code) in float32, rounded once (dense.py:125-139, the floats of a prompt chunk). */
+SC_API int sc_scaled_matvec(const void* codes, const void* scales, const void* d, int rows, int cols, int d_step,
+                            const void* x, int dtype, int tokens, void* out, void* stream);
+SC_API int sc_scaled_floats(const void* codes, const void* scales, const void* d, int rows, int cols, int d_step,
+                            int out_dtype, void* out, void* stream);
+
 /* One MoE block in decode, strata_mlx/fused.py:487-497 (_Routed.__call__): the router (fused.py:377-390), top_k
  * (:424-436), the softmax over the chosen logits (:491), the routed SwiGLU experts (blocks.py:801-829), the
  * shared expert and its gate, and moe_combine (fused.py:467-481), for a window of 1..8 tokens. */

@@ -50,6 +50,8 @@ SIGNATURES = {
     "sc_tile_matmul_path": (_I, [_I, _I, _I, _I, _I, _I, _P, _P]),
     "sc_tile_glu": (_I, [_I, _P, _I, _P, _I, _P, _I, _I, _I, _P, _I, _I, _P, _P, _I, _P, _P, _SZ, _P, _P]),
     "sc_tile_glu_workspace": (_SZ, [_I, _I, _I]),
+    "sc_scaled_matvec": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _P]),
+    "sc_scaled_floats": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "sc_moe_decode_layer": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_workspace": (_SZ, [_P, _I]),
     "sc_moe_decode_routes": (_I, [_P, _I, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
