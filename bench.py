@@ -522,6 +522,46 @@ def window_stream(layers, device, tokens: int = 8, reps: int = 20) -> dict:
             "tok_per_s": tokens / (us * 1e-6)}
 
 
+def dense_stream(device, n_layers: int = 24, rows: int = 4096, cols: int = 4096, reps: int = 20) -> dict:
+    """The Q6_K dense layer (dense.ScaledLinear, strata_mlx/dense.py:109-167) of a one-token window through
+    `n_layers` distinct 4096 x 4096 layers in turn, replayed as a CUDA graph (codes 16 MB a layer: the step reads
+    HBM, not L2). Synthetic parts (codes in [-32, 31], scales, d) made on the device. Algorithmic bytes: codes,
+    scales and d of every layer, the activations and outputs."""
+    from strata_mlx_b200.dense import ScaledLinear
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    lins = []
+    for _ in range(n_layers):
+        codes = torch.randint(-32, 32, (rows, cols), generator=gen, device=device, dtype=torch.int8)
+        scales = torch.randint(-128, 128, (rows, cols // 16), generator=gen, device=device, dtype=torch.int8)
+        d = (torch.randn((rows, cols // 256), generator=gen, device=device) * 1e-3).half()
+        lins.append(ScaledLinear(codes, scales, d))
+    x = torch.randn((1, cols), generator=gen, device=device).to(torch.bfloat16)
+    s = torch.cuda.Stream(device=device)
+    with torch.cuda.stream(s):
+        for lin in lins:
+            lin(x)
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()  # the layers replayed as a graph: host launches would set the pace otherwise
+    with torch.cuda.graph(graph, stream=s):
+        for lin in lins:
+            lin(x)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        graph.replay()
+        e0.record(s)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n_layers)
+    nbytes = lins[0].nbytes + cols * 2 + rows * 2
+    return {"api": "strata_mlx_b200.dense.ScaledLinear.__call__ (Q6_K parts, one token, 24 layers in turn, graph)",
+            "rows": rows, "cols": cols, "bytes_per_launch": nbytes, "us_per_launch": us,
+            "gbs": nbytes / (us * 1e-6) / 1e9}
+
+
 def time_stages(layers, graph, device, reps: int, capture: bool) -> dict:
     """Each of the fused path's three kernels alone: one launch per layer on the workspace the last step left,
     48 launches (with their programmatic dependencies) replayed as a graph, timed with CUDA events on its stream."""
@@ -765,6 +805,10 @@ def main() -> None:
         st["frac"] = st["gbs"] / pk["hbm_gbs"]
         st["peak"] = pk["hbm_gbs"]
         line["window8_stream"] = st
+        ds = dense_stream(device)
+        ds["frac"] = ds["gbs"] / pk["hbm_gbs"]
+        ds["peak"] = pk["hbm_gbs"]
+        line["dense_stream"] = ds
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cb = cpu_sample(args.kinds, 12.0, True)
         cpu_ms = step_seconds(cb["per_layer_s"], args.layers, args.kinds) * 1000.0
