@@ -89,6 +89,8 @@ class ScaledLinear:
                 _holding.append(self)
             return x @ self._floats.T
         xs = _contig(x.reshape(tokens, cols))
+        if xs.data_ptr() % 16:  # a view at an odd offset: the kernels load the activations 16 bytes at a time
+            xs = xs.clone()
         out = torch.empty((tokens, rows), dtype=x.dtype, device=x.device)
         check(_lib.lib().sc_scaled_matvec(ptr(self.codes), ptr(self.scales), ptr(self.d), rows, cols, self.d_step,
                                           ptr(xs), _dtype(xs), tokens, ptr(out), stream()), "scaled_matvec")

@@ -51,6 +51,12 @@ def test_a_window_multiplies_as_the_weights_do(cuda, tokens, dtype):
     assert np.abs(got.float().cpu().numpy() - want).max() <= TOL[dtype] * np.abs(want).max()
 
 
+def test_activations_at_an_odd_offset(cuda):
+    lin = linear(q6k(9))
+    x = randn((3 * COLS + 1,), torch.bfloat16, 8)[1:].reshape(3, COLS)  # contiguous, 2 bytes past 16
+    assert torch.equal(lin(x), lin(x.contiguous().clone()))
+
+
 @pytest.mark.parametrize("tokens", [1, 4, MAX_TOKENS + 4])
 def test_reordered_outputs_and_inputs(cuda, tokens):
     t = q6k(7)
