@@ -138,24 +138,27 @@ class Clocks:
 # ---- the workload
 
 
-def build_layers(n_layers: int, mode: str, rank: int, device):
+def build_layers(n_layers: int, mode: str, rank: int, device, first: int = 0):
+    """The chain's layers on one device, every expert: the same model as build_ep_layers makes (seeds of the layer
+    index only, EP_SIGMA scales), layers [first, first + n_layers)."""
     from strata_mlx_b200 import blocks as B
     from strata_mlx_b200 import fused as F
     from strata_mlx_b200.synthetic import blocks_cuda
 
     layers = []
-    for l in range(n_layers):
+    for l in range(first, first + n_layers):
         kind = kind_of(l, mode)
-        seed = 1000 * rank + 10 * l
+        seed = 10 * l
+        sig = EP_SIGMA.get(kind, 0.02)
         g = torch.Generator(device=device)
         g.manual_seed(seed + 7)
         lin = {
-            "gate": B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, seed + 1, device), kind, (E, I, H)),
-            "up": B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, seed + 2, device), kind, (E, I, H)),
-            "down": B.BlockSwitchLinear(blocks_cuda(kind, E, H, I, seed + 3, device), kind, (E, H, I)),
-            "sgate": B.BlockSwitchLinear(blocks_cuda(kind, 1, IS, H, seed + 4, device), kind, (1, IS, H)),
-            "sup": B.BlockSwitchLinear(blocks_cuda(kind, 1, IS, H, seed + 5, device), kind, (1, IS, H)),
-            "sdown": B.BlockSwitchLinear(blocks_cuda(kind, 1, H, IS, seed + 6, device), kind, (1, H, IS)),
+            "gate": B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, seed + 1, device, sigma=sig), kind, (E, I, H)),
+            "up": B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, seed + 2, device, sigma=sig), kind, (E, I, H)),
+            "down": B.BlockSwitchLinear(blocks_cuda(kind, E, H, I, seed + 3, device, sigma=sig), kind, (E, H, I)),
+            "sgate": B.BlockSwitchLinear(blocks_cuda(kind, 1, IS, H, seed + 4, device, sigma=sig), kind, (1, IS, H)),
+            "sup": B.BlockSwitchLinear(blocks_cuda(kind, 1, IS, H, seed + 5, device, sigma=sig), kind, (1, IS, H)),
+            "sdown": B.BlockSwitchLinear(blocks_cuda(kind, 1, H, IS, seed + 6, device, sigma=sig), kind, (1, H, IS)),
         }
         router = (torch.randn((E, H), generator=g, device=device) * 0.02).half()
         sgw = (torch.randn((H,), generator=g, device=device) * 0.02).half()
@@ -206,6 +209,41 @@ def build_ep_layers(n_layers: int, mode: str, rank: int, world: int, device):
     return layers
 
 
+def ep_parity(layers, eager, x_in, refeed: int, args, world: int, rank: int, device, cs) -> bool | None:
+    """Bit-identity of the expert-parallel chain with one device, checked on every rank before anything is timed:
+    for 3 steps, this rank's output of the chain (eager) against the single-device MoEDecodeLayer (every expert) on
+    the window of all ranks' tokens. With refeed r the chain's output depends only on its last r layers (each
+    segment starts again from the step's token), so those are built on one device. Returns the AND over ranks."""
+    import torch.distributed as dist
+
+    if not refeed:
+        return None
+    ref = build_layers(refeed, args.kinds, rank, device, first=len(layers) - refeed)
+    windows = []
+    for r in range(world):  # every rank's tokens, made as that rank makes them
+        g = torch.Generator(device=device)
+        g.manual_seed(99 + r)
+        windows.append(torch.randn((3, H), generator=g, device=device).to(torch.bfloat16))
+    ok = True
+    with torch.cuda.stream(cs):
+        for i in range(3):
+            x_in.copy_(windows[rank][i : i + 1])
+            got = eager().clone()
+            X = torch.cat([w[i : i + 1] for w in windows])
+            y = X
+            for l in ref:
+                y = l(y)
+            ok = ok and bool(torch.equal(got.reshape(1, H), y[rank : rank + 1]))
+    torch.cuda.synchronize()
+    for l in ref:
+        l.check_errors()
+    del ref
+    torch.cuda.empty_cache()
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
 def run_ep(args, world, rank, local) -> None:
     """N > 1: expert parallel decode, one token per rank per step through the chain; the exchange of each layer is
     an NCCL all-gather and all-reduce (strata_mlx_b200/ep.py)."""
@@ -248,6 +286,7 @@ def run_ep(args, world, rank, local) -> None:
     torch.cuda.current_stream().wait_stream(cs)
     torch.cuda.synchronize()
     barrier(world)
+    bits_same = ep_parity(layers, eager, x_in, refeed, args, world, rank, device, cs)
     graph = None
     if not args.no_graph:
         graph = torch.cuda.CUDAGraph()
@@ -306,6 +345,10 @@ def run_ep(args, world, rank, local) -> None:
     cfg["refeed"] = refeed
     cfg["expert_sigma"] = EP_SIGMA
     cfg["outputs_finite"] = finite
+    cfg["ep_bits_same"] = bits_same
+    cfg["ep_bits_same_how"] = (f"before timing, 3 steps of the chain on every rank against the single-device decode "
+                               f"block (all 512 experts) on the window of every rank's tokens, through the last "
+                               f"{refeed}-layer segment the chain's output depends on")
     cfg["parallelism"] = (f"ep{world}: experts sharded over ranks, the exchange in the kernels over peer memory "
                           "(NVLink stores, release/acquire counts)" if chain is not None else
                           f"ep{world}: experts sharded over ranks, NCCL all-gather + all-reduce per layer")
@@ -336,26 +379,17 @@ def run_ep(args, world, rank, local) -> None:
 
 # ---- configuration 3: the prefill grouped expert GEMM (--workload prefill)
 
-PREFILL_TOKENS, ZIPF_S = 2048, 0.8
 PREFILL_KIND = "IQ3_XXS"
 
 
-def prefill_routes():
-    """2,048 tokens' top-10 of 512 experts from logits N(0,1) - s ln(rank_e) over a seeded permutation of ranks
-    (s = 0.8: 364 experts used, as many as the reference's real layers use)."""
-    rng = np.random.default_rng(2048)
-    logits = rng.standard_normal((PREFILL_TOKENS, E)) - ZIPF_S * np.log(rng.permutation(E) + 1)
-    return np.argsort(-logits, axis=1, kind="stable")[:, :K].astype(np.int32)
-
-
-def run_prefill(args, world, rank) -> None:
+def prefill_result(steps: int, warmup: int, cpu_seconds: float | None) -> dict:
     """Configuration 3 on one GPU: a prefill chunk's 20,480 (token, expert) pairs through switch_glu's tiled
     path (tiles_of, the gate / up / down tile products on tcgen05, swiglu), IQ3_XXS experts, bf16 in, fp32 sums.
     `value`: TFLOP/s on the pairs' 6 * pairs * H * I flops; roofline: the gate product's kernel alone against the
-    measured bf16 tensor peak."""
+    measured bf16 tensor peak (burst: the kernel is timed alone). cpu_seconds None: no CPU baseline."""
     from strata_mlx_b200 import _lib
     from strata_mlx_b200 import blocks as B
-    from strata_mlx_b200.synthetic import blocks_cuda
+    from strata_mlx_b200.synthetic import PREFILL_TOKENS, ZIPF_S, blocks_cuda, prefill_routes
 
     _lib.load()
     device = torch.device("cuda", torch.cuda.current_device())
@@ -372,18 +406,18 @@ def run_prefill(args, world, rank) -> None:
     pairs = PREFILL_TOKENS * K
     flops = 6.0 * pairs * H * I
     s = torch.cuda.current_stream()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         B.switch_glu(x, idx, up, gate, down)
     torch.cuda.synchronize()
-    clocks = Clocks(0)
+    clocks = Clocks(device.index)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
-    for _ in range(args.steps):
+    for _ in range(steps):
         B.switch_glu(x, idx, up, gate, down)
     e1.record(s)
     torch.cuda.synchronize()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / steps
     _lib.check_device_errors(device)
 
     # the gate product's kernel alone (the dominant kernel: the three products are alike in flops)
@@ -402,14 +436,14 @@ def run_prefill(args, world, rank) -> None:
     k_tflops = 2.0 * pairs * I * H / (k_ms * 1e-3) / 1e12
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            tpk, src = float(json.load(f)["bf16_tflops"]), "measured"
+            tpk, src = float(json.load(f)["bf16_tflops"]), "measured (burst)"
     except Exception:
         tpk, src = 1590.0, "fallback"
 
     # e2e: the reference's call (switch_glu) from pinned host activations, the pairs' outputs back to the host
     # (pinned host buffers both ways)
     host_x = x.cpu().pin_memory()
-    e2e_steps = min(args.steps, 10)
+    e2e_steps = min(steps, 10)
     out = B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down)
     host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     host_out.copy_(out, non_blocking=True)
@@ -419,32 +453,130 @@ def run_prefill(args, world, rank) -> None:
         host_out.copy_(B.switch_glu(host_x.to(device, non_blocking=True), idx, up, gate, down), non_blocking=True)
     torch.cuda.synchronize(device)
     e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1000.0
-    out = host_out
+    res = {"metric": "prefill grouped expert GEMM TFLOP/s (config 3)", "value": flops / (ms * 1e-3) / 1e12,
+           "unit": "TFLOP/s", "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
+           "dtype": "bf16", "data": "synthetic: seeded IQ3_XXS blocks made in HBM, seeded Zipf-skewed routes",
+           "config": {"workload": "config3: prefill grouped expert GEMM, 2048-token chunk, top-10 of 512 experts "
+                                  "(hidden 2048, SwiGLU inter 512), IQ3_XXS, bf16 in / fp32 accumulate",
+                      "pairs": pairs, "experts_used": int((counts > 0).sum()), "max_pairs_per_expert": int(counts.max()),
+                      "median_pairs_per_used_expert": float(np.median(counts[counts > 0])), "zipf_s": ZIPF_S,
+                      "flops_per_step": flops,
+                      "l2": "inputs larger than L2: 3 x 401 MB of expert blocks, ~360 experts' share read per step"},
+           "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                   "h2d_bytes_per_step": PREFILL_TOKENS * H * 2, "d2h_bytes_per_step": int(host_out.numel()) * 2,
+                   "api": "strata_mlx_b200.blocks.switch_glu"},
+           "roofline": {"bound": "tensor", "kernel": "tile_mma_kernel (the gate product, 512 x 2048)",
+                        "achieved": k_tflops, "peak": tpk, "unit": "TFLOP/s", "frac": k_tflops / tpk,
+                        "peak_source": src, "traffic": None, "us_per_launch": k_ms * 1e3},
+           # per step: tiles_of, slot_pairs, the gate / up products, swiglu, the down product
+           "gpu_launches": 6 * steps, "gpu_launches_per_step": 6, "clocks": clk}
+    if cpu_seconds:
+        res["cpu_baseline"] = prefill_cpu_sample(pairs, flops, cpu_seconds)
+    del gate, up, down
+    torch.cuda.empty_cache()
+    return res
 
-    line = {"metric": "prefill grouped expert GEMM TFLOP/s (config 3)", "value": flops / (ms * 1e-3) / 1e12,
-            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded IQ3_XXS blocks made in HBM, seeded Zipf-skewed routes",
-            "config": {"workload": "config3: prefill grouped expert GEMM, 2048-token chunk, top-10 of 512 experts "
-                                   "(hidden 2048, SwiGLU inter 512), IQ3_XXS, bf16 in / fp32 accumulate",
-                       "pairs": pairs, "experts_used": int((counts > 0).sum()), "max_pairs_per_expert": int(counts.max()),
-                       "median_pairs_per_used_expert": float(np.median(counts[counts > 0])), "zipf_s": ZIPF_S,
-                       "flops_per_step": flops,
-                       "l2": "inputs larger than L2: 3 x 401 MB of expert blocks, 364 experts' share read per step"},
-            "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": PREFILL_TOKENS * H * 2, "d2h_bytes_per_step": int(out.numel()) * 2,
-                    "api": "strata_mlx_b200.blocks.switch_glu"},
-            "roofline": {"bound": "tensor", "kernel": "tile_mma_kernel (the gate product, 512 x 2048)",
-                         "achieved": k_tflops, "peak": tpk, "unit": "TFLOP/s", "frac": k_tflops / tpk,
-                         "peak_source": src, "traffic": None, "us_per_launch": k_ms * 1e3},
-            # per step: tiles_of, slot_pairs, the gate / up products, swiglu, the down product
-            "gpu_launches": 6 * args.steps, "gpu_launches_per_step": 6, "clocks": clk}
-    if not args.no_cpu_baseline:
-        line["cpu_baseline"] = prefill_cpu_sample(pairs, flops)
+
+def run_prefill(args, world, rank) -> None:
+    """--workload prefill: configuration 3 as a line of its own."""
+    res = prefill_result(args.steps, args.warmup, None if args.no_cpu_baseline else 10.0)
+    line = {"metric": res.pop("metric"), "value": res.pop("value"), "unit": res.pop("unit"), "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "scaling": "weak", "vs_baseline": None, **res}
     print(json.dumps(line), flush=True)
 
 
-def prefill_cpu_sample(pairs: int, flops: float) -> dict:
+# ---- configuration 1 (BASELINE configs[0]): one IQ3_S SwiGLU expert, float32 activations, batch 1
+
+C1_KIND, C1_COPIES = "IQ3_S", 256
+
+
+def config1_result(reps: int = 20, cpu_seconds: float = 5.0) -> dict:
+    """One SwiGLU expert (gate / up 2048 -> 512, down 512 -> 2048) as IQ3_S blocks, x float32 N(0, 1), batch 1,
+    through the reference's call (switch_glu of one token and one expert: gate and up products, swiglu, down).
+    C1_COPIES distinct copies of the expert (346 MB, more than L2) are called in turn, the calls replayed as a CUDA
+    graph. Bytes per call: the expert's 1,351,680 B of blocks."""
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200.synthetic import blocks_cuda
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    gate = B.BlockSwitchLinear(blocks_cuda(C1_KIND, C1_COPIES, I, H, 41, device), C1_KIND, (C1_COPIES, I, H))
+    up = B.BlockSwitchLinear(blocks_cuda(C1_KIND, C1_COPIES, I, H, 42, device), C1_KIND, (C1_COPIES, I, H))
+    down = B.BlockSwitchLinear(blocks_cuda(C1_KIND, C1_COPIES, H, I, 43, device), C1_KIND, (C1_COPIES, H, I))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1)
+    x = torch.randn((1, H), generator=gen, device=device)
+    ids = [torch.tensor([[e]], dtype=torch.int32, device=device) for e in range(C1_COPIES)]
+    nbytes = 2 * I * row_bytes(C1_KIND, H) + H * row_bytes(C1_KIND, I)
+    st = torch.cuda.Stream(device=device)
+    with torch.cuda.stream(st):
+        for e in range(C1_COPIES):
+            B.switch_glu(x, ids[e], up, gate, down)
+    st.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for e in range(C1_COPIES):
+            out = B.switch_glu(x, ids[e], up, gate, down)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        g.replay()
+        e0.record(st)
+        for _ in range(reps):
+            g.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * C1_COPIES)
+    # e2e: the token from pinned host memory, the call, the result back to pinned host memory
+    hx = x.cpu().pin_memory()
+    ho = torch.empty((1, H), dtype=torch.float32).pin_memory()
+    for e in range(3):
+        ho.copy_(B.switch_glu(hx.to(device, non_blocking=True), ids[e], up, gate, down).reshape(1, H), non_blocking=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    n_e2e = 200
+    for i in range(n_e2e):
+        ho.copy_(B.switch_glu(hx.to(device, non_blocking=True), ids[i % C1_COPIES], up, gate, down).reshape(1, H),
+                 non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_us = (time.perf_counter() - t0) / n_e2e * 1e6
+    pk = peaks()
+    res = {"workload": "config1: one SwiGLU expert (gate/up 2048->512, down 512->2048) as IQ3_S blocks, x float32 "
+                       "N(0,1), batch 1, through blocks.switch_glu",
+           "bytes_per_call": nbytes, "us_per_call": us, "gbs": nbytes / (us * 1e-6) / 1e9,
+           "roofline": {"bound": "hbm", "achieved": nbytes / (us * 1e-6) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": nbytes / (us * 1e-6) / 1e9 / pk["hbm_gbs"], "peak_source": pk["source"]},
+           "e2e": {"us_per_call": e2e_us, "gbs": nbytes / (e2e_us * 1e-6) / 1e9, "h2d_bytes_per_step": H * 4,
+                   "d2h_bytes_per_step": H * 4, "api": "strata_mlx_b200.blocks.switch_glu"},
+           "l2": f"{C1_COPIES} distinct copies of the expert called in turn ({C1_COPIES * nbytes / 1e6:.0f} MB > L2)",
+           "gpu_launches_per_call": 4}
+    if cpu_seconds:
+        from oracle import cref
+        from strata_mlx_b200.synthetic import blocks_numpy
+
+        threads = cref.threads(os.cpu_count() or 1)
+        rng = np.random.default_rng(0)
+        k = cref.KINDS[C1_KIND]
+        wg, wu = blocks_numpy(C1_KIND, 1, I, H, rng), blocks_numpy(C1_KIND, 1, I, H, rng)
+        wd = blocks_numpy(C1_KIND, 1, H, I, rng)
+        xx = rng.standard_normal(H).astype(np.float32)
+        og, ou, od = np.empty(I, np.float32), np.empty(I, np.float32), np.empty(H, np.float32)
+        lib = cref.lib()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < cpu_seconds or n < 3:
+            lib.ref_matvec(k, wg.ctypes.data, I, H, xx.ctypes.data, og.ctypes.data)
+            lib.ref_matvec(k, wu.ctypes.data, I, H, xx.ctypes.data, ou.ctypes.data)
+            h = (og / (1 + np.exp(-og)) * ou).astype(np.float32)
+            lib.ref_matvec(k, wd.ctypes.data, H, I, h.ctypes.data, od.ctypes.data)
+            n += 1
+        cus = (time.perf_counter() - t0) / n * 1e6
+        res["cpu_baseline"] = {"value": nbytes / (cus * 1e-6) / 1e9, "unit": "GB/s", "us_per_call": cus,
+                               "cores": threads, "kind": "port",
+                               "sample": f"{n} calls of the C oracle (decode + float32 matvec, OpenMP) in ~{cpu_seconds:.0f} s"}
+    del gate, up, down, g
+    torch.cuda.empty_cache()
+    return res
+
+
+def prefill_cpu_sample(pairs: int, flops: float, seconds: float = 10.0) -> dict:
     """The C oracle (decode + float32 matvec per pair, all host cores) on a bounded sample of pairs of the same
     shapes, scaled to the step's pairs."""
     from oracle import cref
@@ -460,13 +592,13 @@ def prefill_cpu_sample(pairs: int, flops: float) -> dict:
     h = rng.standard_normal(I).astype(np.float32)
     og, od = np.empty(I, np.float32), np.empty(H, np.float32)
     n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < 10.0 or n < 3:
+    while time.perf_counter() - t0 < seconds or n < 3:
         for w, xin, o, r, c in ((w_gu, x, og, I, H), (w_gu, x, og, I, H), (w_d, h, od, H, I)):
             lib.ref_matvec(k, w.ctypes.data, r, c, xin.ctypes.data, o.ctypes.data)
         n += 1
     per_pair = (time.perf_counter() - t0) / n
     return {"value": flops / (per_pair * pairs) / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{n} pairs' gate, up and down products timed (~10 s), scaled to {pairs} pairs"}
+            "sample": f"{n} pairs' gate, up and down products timed (~{seconds:.0f} s), scaled to {pairs} pairs"}
 
 
 def stage_bytes(kind: str) -> dict:
@@ -690,7 +822,8 @@ def workload_config(args, world) -> dict:
     return {"workload": "config2: one MoE layer decode, batch 1 per rank (hidden 2048, 512 experts x SwiGLU inter 512, "
                         "top-10 softmax router, shared expert inter 512), experts "
                         + ("Q2_0 / IQ3_S alternating" if args.kinds == "mixed" else args.kinds)
-                        + f", chained over {args.layers} distinct layers",
+                        + f", chained over {args.layers} distinct layers (a layer takes the previous one's output; "
+                        f"the step's token is fed again every {EP_REFEED} layers)",
             "layers": args.layers, "tokens_per_rank_per_step": 1, "hidden": H, "experts": E, "inter": I, "top_k": K,
             "shared_inter": IS, "global_batch": world, "parallelism": "replicas" if world > 1 else "single",
             "l2": "inputs larger than L2: ~0.6 GB of distinct routed-expert blocks per step, a fresh token each step"}
@@ -707,6 +840,8 @@ def main() -> None:
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="leave out the configuration-1 and configuration-3 sub-lines of the one-GPU decode line")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the layers one by one instead of replaying a CUDA graph (for profilers that cannot "
                          "follow a stream capture); the same kernels run")
@@ -740,7 +875,8 @@ def main() -> None:
     _lib.load()
     device = torch.device("cuda", torch.cuda.current_device())
     layers = build_layers(args.layers, args.kinds, rank, device)
-    graph = F.DecodeGraph(layers, tokens=1, device=device, capture=not args.no_graph)
+    refeed = EP_REFEED if args.layers % EP_REFEED == 0 else 0
+    graph = F.DecodeGraph(layers, tokens=1, device=device, capture=not args.no_graph, chain=True, refeed=refeed)
     gen = torch.Generator(device=device)
     gen.manual_seed(99 + rank)
     n_tok = args.steps + args.warmup
@@ -785,10 +921,13 @@ def main() -> None:
     achieved = gu["gbs"]
     traffic = read_traffic([l.kind for l in layers])
 
+    finite = bool(torch.isfinite(graph.outs[-1].float()).all().item())
+    cfg = workload_config(args, world)
+    cfg.update(refeed=refeed, expert_sigma=EP_SIGMA, outputs_finite=finite)
     line = {"metric": METRIC, "value": world * 1000.0 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic: seeded GGUF blocks and float16 router made in HBM",
-            "config": workload_config(args, world),
+            "config": cfg,
             "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tok/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2,
                     "api": "strata_mlx_b200.fused.DecodeGraph.__call__"},
             "roofline": {"bound": "hbm", "kernel": "gate_up_kernel (routed + shared experts' gate/up/swiglu)",
@@ -809,6 +948,11 @@ def main() -> None:
         ds["frac"] = ds["gbs"] / pk["hbm_gbs"]
         ds["peak"] = pk["hbm_gbs"]
         line["dense_stream"] = ds
+    if world == 1 and not args.no_extra:
+        del graph
+        torch.cuda.synchronize()
+        line["config1"] = config1_result(cpu_seconds=None if args.no_cpu_baseline else 5.0)
+        line["prefill"] = prefill_result(20, 5, None if args.no_cpu_baseline else 6.0)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cb = cpu_sample(args.kinds, 12.0, True)
         cpu_ms = step_seconds(cb["per_layer_s"], args.layers, args.kinds) * 1000.0

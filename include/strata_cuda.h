@@ -165,9 +165,11 @@ SC_API size_t sc_tile_glu_workspace(int P, int inter, int a_dtype);
  * rows by 4 and cols by 256 (dense.py:97-99 fits), d_step a multiple of 16 dividing cols; codes and x 16-byte
  * aligned. sc_scaled_matvec: out (tokens, rows) = x (tokens, cols) . W^T in x's type, float32 sums, tokens <= 8
  * (dense.py:141-167, the window kernel). sc_scaled_floats: W (rows, cols) in out_dtype, each weight
- * float(d) * float(scale) * float(code) in float32, rounded once (dense.py:125-139, the floats of a prompt chunk). */
+ * float(d) * float(scale) * float(code) in float32, rounded once (dense.py:125-139, the floats of a prompt chunk).
+ * err: device int in which the tensor-core window kernel records SC_ERR_TIMEOUT when one of its bounded waits for
+ * a bulk copy gives up (its rows are then left unwritten); may be NULL. */
 SC_API int sc_scaled_matvec(const void* codes, const void* scales, const void* d, int rows, int cols, int d_step,
-                            const void* x, int dtype, int tokens, void* out, void* stream);
+                            const void* x, int dtype, int tokens, void* out, int* err, void* stream);
 SC_API int sc_scaled_floats(const void* codes, const void* scales, const void* d, int rows, int cols, int d_step,
                             int out_dtype, void* out, void* stream);
 
@@ -266,6 +268,12 @@ SC_API int sc_ep_combine(const sc_moe_layer* layer, const sc_ep_exchange* ex, in
  * be issued. Same results as sc_moe_decode_layer, bit for bit. */
 #define SC_NOALLOC_SCRATCH_BYTES (4u << 20)
 SC_API int sc_moe_decode_layer_noalloc(const sc_moe_layer* layer, const void* x, int tokens, void* out, void* stream);
+
+/* The error word of sc_moe_decode_layer_noalloc's kernels on the current device (no counterpart in strata-mlx). The
+ * kernels of a call record a bad expert id or a bounded wait that gave up in the static array's first int, which no
+ * caller can reach otherwise. This waits for `stream`, stores in *code the first error recorded since the last read
+ * (SC_OK when none), and clears the word. Allocates nothing. */
+SC_API int sc_moe_decode_noalloc_error(int* code, void* stream);
 
 #ifdef __cplusplus
 }

@@ -278,6 +278,20 @@ def softmax_topk(logits: np.ndarray, idx: np.ndarray) -> np.ndarray:
 def moe_combine(y: np.ndarray, w: np.ndarray, g: np.ndarray, s: np.ndarray, dtype) -> np.ndarray:
     """strata_mlx/fused.py:448-481: OutT(sum_k y_k*w_k) + OutT(OutT(sigmoid(g)) * s), the products of each token
     added in MLX's col_reduce order: 8 partial sums (partial j takes k = j, j+8, ...), then in order."""
+    return moe_combine_parts(y, w, g, s, dtype)["out"]
+
+
+def gate_of(g: np.ndarray, dtype) -> np.ndarray:
+    """The shared expert's gate as the combine uses it (fused.py:493): sigmoid in float32, rounded to the type."""
+    gg = np.asarray(g, dtype=F32)
+    with np.errstate(over="ignore"):
+        return round_to(F32(1) / (F32(1) + np.exp(-gg).astype(F32)), dtype)
+
+
+def moe_combine_parts(y: np.ndarray, w: np.ndarray, g: np.ndarray, s: np.ndarray, dtype, gate=None) -> dict:
+    """moe_combine with its two rounded terms: {"out", "routed" = OutT(sum_k y_k w_k), "shared" = OutT(gate * s),
+    "gate" = OutT(sigmoid(g))}, each (tokens, D) (gate (tokens, 1)). `gate`, when given, replaces the sigmoid's
+    rounded value (a test's alternative for a gate on a rounding edge)."""
     y = np.asarray(y, dtype=F32)
     w = np.asarray(w, dtype=F32)
     *lead, K, D = y.shape
@@ -290,10 +304,13 @@ def moe_combine(y: np.ndarray, w: np.ndarray, g: np.ndarray, s: np.ndarray, dtyp
             part = (yy[:, k] * ww[:, k : k + 1]).astype(F32) + part  # contraction off: product rounded first
         acc = part if j == 0 else (part + acc).astype(F32)
     routed = round_to(acc, dtype)
-    gg = np.asarray(g, dtype=F32).reshape(-1, 1)
-    gate = round_to(F32(1) / (F32(1) + np.exp(-gg).astype(F32)), dtype)
+    if gate is None:
+        gate = gate_of(np.asarray(g, dtype=F32).reshape(-1, 1), dtype)
+    gate = np.asarray(gate, dtype=F32).reshape(-1, 1)
     shared = round_to(gate * np.asarray(s, dtype=F32).reshape(-1, D), dtype)
-    return round_to(routed + shared, dtype).reshape(*lead, D)
+    out = round_to(routed + shared, dtype)
+    return {"out": out.reshape(*lead, D), "routed": routed.reshape(*lead, D), "shared": shared.reshape(*lead, D),
+            "gate": gate}
 
 
 TOKENS_TILE = 16  # strata_mlx/blocks.py:463
@@ -353,3 +370,47 @@ def moe_layer(x, router_w, shared_gate_w, gate, up, down, sgate, sup, sdown, k: 
         s = np.zeros((T, H), dtype=F32)
         gs = np.full(T, -np.inf, dtype=F32)
     return moe_combine(y, wts, gs, s, dtype), idx, wts
+
+
+def expert_rows(blocks: np.ndarray, kind: str, e: int, rows: int, cols: int) -> np.ndarray:
+    """Expert e of a (experts, rows, cols) stack of blocks, dequantized: (rows, cols) float32."""
+    rb = row_bytes(kind, cols)
+    return dequantize(np.asarray(blocks)[e * rows * rb : (e + 1) * rows * rb], kind, (rows, cols))
+
+
+def moe_layer_blocks(x, L: dict, hidden: int, inter: int, k: int, dtype, shared_inter: int = 0) -> dict:
+    """moe_layer on a layer given as blocks (synthetic.layer_numpy's dict), dequantizing only the experts the window
+    chose: bounded work at benchmark sizes (512 experts). Returns {"out", "idx", "w", "routed", "shared", "gate",
+    "s", "y", "gs"}: the output, the routes, and the combine's inputs and rounded terms (moe_combine_parts)."""
+    kg, ku, kd = L["kinds"]
+    x = round_to(x, dtype)
+    T, H = x.shape
+    logits = router(L["router"], x).astype(F32)
+    idx = top_k(logits, k)
+    wts = softmax_topk(logits, idx)
+    y = np.zeros((T, k, H), dtype=F32)
+    for e in np.unique(idx):
+        wg, wu = expert_rows(L["gate"], kg, e, inter, H), expert_rows(L["up"], ku, e, inter, H)
+        wd = expert_rows(L["down"], kd, e, H, inter)
+        for t, j in zip(*np.nonzero(idx == e)):
+            xt = x[t].astype(np.float64)
+            g = round_to((wg.astype(np.float64) @ xt).astype(F32), dtype)
+            u = round_to((wu.astype(np.float64) @ xt).astype(F32), dtype)
+            h = swiglu(g, u, dtype)
+            y[t, j] = round_to((wd.astype(np.float64) @ h.astype(np.float64)).astype(F32), dtype)
+    if shared_inter:
+        sk = L.get("shared_kinds", L["kinds"])
+        sg = dequantize(L["sgate"], sk[0], (shared_inter, H))
+        su = dequantize(L["sup"], sk[1], (shared_inter, H))
+        sd = dequantize(L["sdown"], sk[2], (H, shared_inter))
+        xd = x.astype(np.float64)
+        h = swiglu(round_to((xd @ sg.T.astype(np.float64)).astype(F32), dtype),
+                   round_to((xd @ su.T.astype(np.float64)).astype(F32), dtype), dtype)
+        s = round_to((h.astype(np.float64) @ sd.T.astype(np.float64)).astype(F32), dtype)
+        gs = round_to(router(L["shared_gate"].reshape(1, -1), x), dtype).reshape(T)
+    else:
+        s = np.zeros((T, H), dtype=F32)
+        gs = np.full(T, -np.inf, dtype=F32)
+    parts = moe_combine_parts(y, wts, gs, s, dtype)
+    parts.update(idx=idx, w=wts, s=s, y=y, gs=gs)
+    return parts

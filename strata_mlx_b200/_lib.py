@@ -50,7 +50,7 @@ SIGNATURES = {
     "sc_tile_matmul_path": (_I, [_I, _I, _I, _I, _I, _I, _P, _P]),
     "sc_tile_glu": (_I, [_I, _P, _I, _P, _I, _P, _I, _I, _I, _P, _I, _I, _P, _P, _I, _P, _P, _SZ, _P, _P]),
     "sc_tile_glu_workspace": (_SZ, [_I, _I, _I]),
-    "sc_scaled_matvec": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _P]),
+    "sc_scaled_matvec": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _P, _P]),
     "sc_scaled_floats": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "sc_moe_decode_layer": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_workspace": (_SZ, [_P, _I]),
@@ -66,6 +66,7 @@ SIGNATURES = {
     "sc_moe_decode_layer_ep_p2p": (_I, [_P, _P, _I, _I, _I, _P, _SZ, _P]),
     "sc_ep_combine": (_I, [_P, _P, _I, _I, _P, _P, _SZ, _P]),
     "sc_moe_decode_layer_noalloc": (_I, [_P, _P, _I, _P, _P]),
+    "sc_moe_decode_noalloc_error": (_I, [ctypes.POINTER(_I), _P]),
 }
 
 

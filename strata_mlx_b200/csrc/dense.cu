@@ -287,7 +287,7 @@ static int scaled_check(const void* codes, const void* scales, const void* d, in
 }
 
 extern "C" int sc_scaled_matvec(const void* codes, const void* scales, const void* d, int rows, int cols, int d_step,
-                                const void* x, int dtype, int tokens, void* out, void* stream) {
+                                const void* x, int dtype, int tokens, void* out, int* err, void* stream) {
   if (int rc = scaled_check(codes, scales, d, rows, cols, d_step)) return rc;
   if (!x || !out || tokens < 0) return SC_ERR_ARG;
   if (tokens > SC_DENSE_MAX_TOKENS) return SC_ERR_SHAPE;
@@ -304,7 +304,7 @@ extern "C" int sc_scaled_matvec(const void* codes, const void* scales, const voi
           if (e == cudaSuccess)
             kern<<<int(ceil_div(rows, SMMA_ROWS)), SMMA_WARPS * 32, smem, static_cast<cudaStream_t>(stream)>>>(
                 static_cast<const int8_t*>(codes), static_cast<const int8_t*>(scales), static_cast<const __half*>(d),
-                rows, cols, d_step, static_cast<const T*>(x), tokens, static_cast<T*>(out), nullptr);
+                rows, cols, d_step, static_cast<const T*>(x), tokens, static_cast<T*>(out), err);
         }
       });
       if (e != cudaSuccess) return SC_ERR_CUDA;

@@ -71,7 +71,9 @@ static bool chain_forced() {
   return v && v[0] == '1';
 }
 
-static int check_layer(const sc_moe_layer* L, int tokens) {
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int check_layer(const sc_moe_layer* L, int tokens, bool pointers = true) {
   if (!L) return SC_ERR_ARG;
   if (tokens < 1 || tokens > ROUTER_MAX_TOKENS) return SC_ERR_SHAPE;
   if (L->hidden <= 0 || L->inter <= 0 || L->experts <= 0 || L->top_k <= 0 || L->shared_inter < 0) return SC_ERR_SHAPE;
@@ -88,7 +90,24 @@ static int check_layer(const sc_moe_layer* L, int tokens) {
         row_bytes(L->kind_sdown, L->shared_inter) < 0)
       return SC_ERR_SHAPE;
   }
+  // the router rows (and the shared expert's gate) are read 16 bytes at a time on every path
+  if (pointers && (!aligned16(L->router) || (L->shared_inter && !aligned16(L->shared_gate)))) return SC_ERR_ALIGN;
   return SC_OK;
+}
+
+// The fused kernels copy expert rows into shared memory with 1-D bulk copies and read the window 16 bytes at a time:
+// every expert stack and the window must start on 16 bytes (the chain of single-purpose kernels takes any offset).
+static bool v2_aligned(const sc_moe_layer* L, const void* x) {
+  bool ok = aligned16(L->gate) && aligned16(L->up) && aligned16(L->down) && aligned16(x);
+  if (L->shared_inter) ok = ok && aligned16(L->sgate) && aligned16(L->sup) && aligned16(L->sdown);
+  return ok;
+}
+
+// The entry points that only the fused kernels serve: SC_ERR_UNSUPPORTED for a layer they do not take,
+// SC_ERR_ALIGN for one they take at an offset they cannot copy from.
+static int v2_only(const sc_moe_layer* L, const void* x, int tokens) {
+  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  return v2_aligned(L, x) ? SC_OK : SC_ERR_ALIGN;
 }
 
 }  // namespace sc
@@ -96,12 +115,12 @@ static int check_layer(const sc_moe_layer* L, int tokens) {
 using namespace sc;
 
 extern "C" size_t sc_moe_decode_workspace(const sc_moe_layer* layer, int tokens) {
-  if (check_layer(layer, tokens) != SC_OK) return 0;
+  if (check_layer(layer, tokens, false) != SC_OK) return 0;
   return moe_ws(layer, tokens).total;
 }
 
 extern "C" int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_t* idx_offset, size_t* weight_offset) {
-  if (int rc = check_layer(layer, tokens)) return rc;
+  if (int rc = check_layer(layer, tokens, false)) return rc;
   const MoeWs m = moe_ws(layer, tokens);
   if (idx_offset) *idx_offset = m.idx;
   if (weight_offset) *weight_offset = m.w;
@@ -114,7 +133,7 @@ extern "C" int sc_moe_decode_stage(const sc_moe_layer* L, const void* x, int tok
   if (!x || !out || stage < 0 || stage > 2) return SC_ERR_ARG;
   const MoeWs m = moe_ws(L, tokens);
   if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
-  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  if (int rc = v2_only(L, x, tokens)) return rc;
   const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
   return v2_run(L, x, tokens, out, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), stage);
 }
@@ -127,7 +146,7 @@ extern "C" int sc_moe_decode_layer_ep(const sc_moe_layer* L, const void* x, int 
   if (expert_begin < 0 || expert_end <= expert_begin || expert_end > L->experts) return SC_ERR_SHAPE;
   const MoeWs m = moe_ws(L, tokens);
   if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
-  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  if (int rc = v2_only(L, x, tokens)) return rc;
   const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
   V2Ep ep;
   ep.e0 = expert_begin;
@@ -147,7 +166,8 @@ extern "C" int sc_moe_decode_layer_ep_p2p(const sc_moe_layer* L, const sc_ep_exc
   if (expert_begin < 0 || expert_end <= expert_begin || expert_end > L->experts) return SC_ERR_SHAPE;
   const MoeWs m = moe_ws(L, tokens);
   if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
-  if (!v2_takes(L, tokens)) return SC_ERR_UNSUPPORTED;
+  const void* window = reinterpret_cast<const void*>(ex->own + ep::xoff(parity, tokens, L->hidden));
+  if (int rc = v2_only(L, window, tokens)) return rc;
   const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
   V2Ep e;
   e.e0 = expert_begin;
@@ -157,7 +177,6 @@ extern "C" int sc_moe_decode_layer_ep_p2p(const sc_moe_layer* L, const sc_ep_exc
   e.rank = ex->rank;
   e.tl = ex->tokens_per_rank;
   e.par = parity;
-  const void* window = reinterpret_cast<const void*>(ex->own + ep::xoff(parity, tokens, L->hidden));
   return v2_run(L, window, tokens, nullptr, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), -1,
                 e);
 }
@@ -225,7 +244,7 @@ extern "C" int sc_moe_decode_layer(const sc_moe_layer* L, const void* x, int tok
   if (!workspace || workspace_bytes < m.total) return SC_ERR_WORKSPACE;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (!chain_forced() && v2_takes(L, tokens)) {
+  if (!chain_forced() && v2_takes(L, tokens) && v2_aligned(L, x)) {
     const V2Offsets o{m.err, m.ticket, m.logits, m.g, m.idx, m.w, m.plan, m.h2, m.sout};
     return v2_run(L, x, tokens, out, ws, o, s);
   }

@@ -49,3 +49,20 @@ extern "C" int sc_moe_decode_layer_noalloc(const sc_moe_layer* layer, const void
   if (!scratch) return SC_ERR_CUDA;
   return sc_moe_decode_layer(layer, x, tokens, out, scratch, SC_NOALLOC_SCRATCH_BYTES, stream);
 }
+
+extern "C" int sc_moe_decode_noalloc_error(int* code, void* stream) {
+  if (!code) return SC_ERR_ARG;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0) return SC_ERR_CUDA;
+  if (device >= kMaxDevices) return SC_ERR_UNSUPPORTED;
+  void* scratch = scratch_address(device);
+  if (!scratch) return SC_ERR_CUDA;
+  // the error word is the scratch's first int (the decode block's workspace layout puts it at offset 0)
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int word = 0;
+  if (cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return SC_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return SC_ERR_CUDA;
+  if (word != 0 && cudaMemsetAsync(scratch, 0, sizeof(int), s) != cudaSuccess) return SC_ERR_CUDA;
+  *code = word;
+  return SC_OK;
+}

@@ -29,26 +29,26 @@ _holding = []  # layers that hold their weights as floats as well, since a promp
 
 
 def release():
-    """Lets go of the float weights made for chunks of prompts (dense.py:88-95)."""
+    """Drops every float copy of a Q6_K layer's weights that a prompt chunk created (dense.py:88-95)."""
     for layer in _holding:
         layer._floats = None
     _holding.clear()
 
 
 def fits(rows: int, cols: int) -> bool:
-    """Whether the kernel takes a layer of this shape (dense.py:97-99)."""
+    """True when the window kernel can run a layer of rows x cols: rows by 4, cols by 256 (dense.py:97-99)."""
     return rows % _ROWS == 0 and cols % (32 * _WEIGHTS) == 0
 
 
 def kept_floats(tensors: dict, itemsize: int = 2) -> int:
-    """Bytes the weights of a file's Q6_K layers take as floats of `itemsize` once a prompt has been read, if they
-    are kept (dense.py:102-106); the output layer never sees a chunk."""
+    """Device bytes that float copies (`itemsize` bytes a weight) of a file's Q6_K layers occupy after a prompt,
+    when the copies are kept; output.weight is left out since prompt chunks never reach it (dense.py:102-106)."""
     return sum(itemsize * t.shape[0] * t.shape[1] for name, t in tensors.items()
                if t.type == "Q6_K" and len(t.shape) == 2 and fits(*t.shape) and name != "output.weight")
 
 
 class ScaledLinear:
-    """A linear layer held as codes, scales and d; called like `nn.Linear` (dense.py:109-167)."""
+    """A Q6_K linear layer stored as its codes, scales and d, used like `nn.Linear` (dense.py:109-167)."""
 
     def __init__(self, codes: torch.Tensor, scales: torch.Tensor, d: torch.Tensor):
         require_cuda(codes, scales, d)
@@ -56,9 +56,9 @@ class ScaledLinear:
             raise ValueError("codes and scales int8, d float16")
         self.codes, self.scales, self.d = _contig(codes), _contig(scales), _contig(d)
         self.output_dims, self.input_dims = (int(v) for v in codes.shape)
-        self.d_step = self.input_dims // int(d.shape[1])  # weights to a d: 256, or fewer where inputs were reordered
+        self.d_step = self.input_dims // int(d.shape[1])  # weights per d value: 256, less after an input reorder
         self._floats = None
-        self.keep = True  # the floats made for a chunk of a prompt stay for the next ones
+        self.keep = True  # reuse the float copy built for one prompt chunk in the chunks after it
         if not fits(*codes.shape):
             raise ValueError(f"a layer of {tuple(codes.shape)} does not fit the kernel")
         if tuple(scales.shape) != (self.output_dims, self.input_dims // 16) or self.input_dims % int(d.shape[1]):
@@ -69,7 +69,7 @@ class ScaledLinear:
         return self.codes.numel() + self.scales.numel() + 2 * self.d.numel()
 
     def floats(self, dtype: torch.dtype) -> torch.Tensor:
-        """The weights (out, in), each worked out in float32 and rounded once to `dtype` (dense.py:125-139)."""
+        """All weights as an (out, in) tensor of `dtype`: d * scale * code in float32, one rounding (dense.py:125-139)."""
         out = torch.empty((self.output_dims, self.input_dims), dtype=dtype, device=self.codes.device)
         check(_lib.lib().sc_scaled_floats(ptr(self.codes), ptr(self.scales), ptr(self.d), self.output_dims,
                                           self.input_dims, self.d_step, DTYPES[dtype], ptr(out), stream()),
@@ -93,32 +93,35 @@ class ScaledLinear:
             xs = xs.clone()
         out = torch.empty((tokens, rows), dtype=x.dtype, device=x.device)
         check(_lib.lib().sc_scaled_matvec(ptr(self.codes), ptr(self.scales), ptr(self.d), rows, cols, self.d_step,
-                                          ptr(xs), _dtype(xs), tokens, ptr(out), stream()), "scaled_matvec")
+                                          ptr(xs), _dtype(xs), tokens, ptr(out), ptr(_lib.error_word(x.device)),
+                                          stream()), "scaled_matvec")
         return out.reshape(*lead, rows)
 
 
 # ---- layers kept as the file's blocks (dense.py:172-244)
 
-AS_BLOCKS = ("Q3_K", "IQ4_XS")  # dense.py:182: the types kept so where experts are read from the SSD
-ARRAY_BYTES = 1.125  # dense.py:183: a weight of these as MLX holds it (a byte, a float16 scale and bias to 32)
+AS_BLOCKS = ("Q3_K", "IQ4_XS")  # dense.py:182: dense types left as blocks when memory is short
+ARRAY_BYTES = 1.125  # dense.py:183: bytes per weight of MLX's 8-bit affine form (code, f16 scale + bias per 32)
 
 
 def as_blocks(t, kinds: tuple = AS_BLOCKS) -> bool:
-    """Whether a dense tensor can stay blocks: of one of `kinds`, and rows that end on a block (dense.py:185-187)."""
-    return t.type in kinds and len(t.shape) == 2 and t.shape[1] % BLOCK[t.type][0] == 0
+    """True for a 2-D tensor of a type in `kinds` whose rows are whole blocks (dense.py:185-187)."""
+    per_block = BLOCK[t.type][0] if t.type in BLOCK else 32 if t.type == "Q8_0" else 0
+    return t.type in kinds and per_block > 0 and len(t.shape) == 2 and t.shape[1] % per_block == 0
 
 
 def spared(tensors: dict) -> int:
-    """Bytes that the dense tensors of a file take less as blocks than as MLX's 8-bit arrays (dense.py:190-194)."""
+    """Bytes saved by holding a file's eligible dense tensors as blocks rather than 8-bit affine arrays; expert
+    stacks and output.weight are not counted (dense.py:190-194)."""
     return sum(int(ARRAY_BYTES * int(np.prod(t.shape))) - t.data.nbytes for name, t in tensors.items()
                if as_blocks(t) and not name.endswith("_exps.weight") and name != "output.weight")
 
 
 class BlockLinear:
-    """A linear layer held as the file's blocks; called like `nn.Linear` (dense.py:197-228).
+    """A linear layer whose weights stay the file's quantized blocks, used like `nn.Linear` (dense.py:197-228).
 
-    `blocks` are the rows in the order of the layer's outputs. `inputs`, if given, is where in the file's row each
-    input is: the blocks cannot be reordered inside, so the activations are, before they multiply."""
+    Row i of `blocks` produces output i. When the loader permuted the layer's inputs, `inputs[j]` gives the file
+    column of input j; a block cannot be split, so the activations are gathered into file order instead."""
 
     def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple, inputs: np.ndarray | None = None):
         require_cuda(blocks)
@@ -141,13 +144,13 @@ class BlockLinear:
             xs = xs.index_select(1, self.to_file)
         if tokens <= MAX_TOKENS:
             out = window_matvec(self.blocks, self.kind, rows, cols, xs)
-        else:  # a chunk of a prompt: the weights dequantized for it and let go
+        else:  # a prompt chunk: dequantize to the activation type for this call only
             out = xs @ dequantize(self.blocks, self.kind, (rows, cols), xs.dtype).T
         return out.reshape(*lead, rows)
 
 
 class BlockEmbedding:
-    """An embedding held as the file's blocks; a token's row is dequantized when the token comes (dense.py:231-244)."""
+    """An embedding table kept as blocks; each lookup dequantizes only the rows of the given ids (dense.py:231-244)."""
 
     def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple, dtype: torch.dtype):
         require_cuda(blocks)

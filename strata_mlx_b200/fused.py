@@ -240,11 +240,14 @@ class MoEDecodeLayer:
 class DecodeGraph:
     """A stack of decode layers (MoEDecodeLayer) replayed as one CUDA graph: the call a serving loop makes per
     decoded window. __call__ takes the window's activations on the host (pinned, or any CPU tensor), copies them
-    in, runs every layer, and returns the last layer's output on the host. `layers` each take the previous
-    layer's input when `chain` is False (each layer reads the window itself), or the previous output when True."""
+    in, runs every layer, and returns the last layer's output on the host. `layers` each take the window itself
+    when `chain` is False, or the previous layer's output when True; with `refeed` = n > 0 (and `chain`), every
+    n-th layer takes the window again -- for a synthetic chain, which has none of the norms a model puts between
+    its MoE blocks and would otherwise grow without bound."""
 
-    def __init__(self, layers: list, tokens: int, device=None, chain: bool = False, capture: bool = True):
-        self.layers, self.tokens, self.chain, self.capture = layers, tokens, chain, capture
+    def __init__(self, layers: list, tokens: int, device=None, chain: bool = False, capture: bool = True,
+                 refeed: int = 0):
+        self.layers, self.tokens, self.chain, self.capture, self.refeed = layers, tokens, chain, capture, refeed
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         H, dt = layers[0].hidden, layers[0].dtype
         self.x = torch.zeros((tokens, H), dtype=dt, device=dev)
@@ -264,7 +267,9 @@ class DecodeGraph:
 
     def run_layers(self) -> None:
         x = self.x
-        for l, o in zip(self.layers, self.outs):
+        for i, (l, o) in enumerate(zip(self.layers, self.outs)):
+            if self.refeed and i % self.refeed == 0:
+                x = self.x
             l(x, out=o)
             if self.chain:
                 x = o

@@ -22,8 +22,8 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-# type id -> (name, weights per block, bytes per block): the GGUF type ids of the formats the reference reads
-# (strata_mlx/gguf.py:25-33)
+# GGUF type id -> (type name, weights in a block, bytes in a block), for the formats strata-mlx reads
+# (strata_mlx/gguf.py:25-33); the ids and block sizes are fixed by the file format
 TYPES = {
     0: ("F32", 1, 4), 1: ("F16", 1, 2), 30: ("BF16", 1, 2),
     2: ("Q4_0", 32, 18), 6: ("Q5_0", 32, 22), 8: ("Q8_0", 32, 34),
@@ -40,15 +40,18 @@ _STRING, _ARRAY = 8, 9
 
 @dataclass
 class Tensor:
+    """One tensor of a GGUF file (the field set of strata_mlx/gguf.py:38-49, which load.py and the tests share)."""
+
     name: str
-    shape: tuple  # numpy order: the last axis is the one a row runs along
-    type: str
-    data: np.ndarray  # the raw bytes, a view into the file
-    path: str = ""  # the file, and where in it the bytes start
-    offset: int = 0
+    shape: tuple  # dimensions outermost first; a row of blocks lies along shape[-1]
+    type: str  # the type's name in TYPES, e.g. "IQ3_S"
+    data: np.ndarray  # uint8 bytes mapped from the file, not copied
+    path: str = ""  # the file that holds the tensor
+    offset: int = 0  # byte offset of `data` inside that file
 
     @property
     def quantized(self) -> bool:
+        """False for the plain float types, True for every block type."""
         return self.type not in ("F32", "F16", "BF16")
 
 

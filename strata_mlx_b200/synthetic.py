@@ -85,3 +85,18 @@ def layer_numpy(rng: np.random.Generator, hidden: int, inter: int, experts: int,
                    sdown=blocks_numpy(sk[2], 1, hidden, shared_inter, rng, sigma),
                    shared_gate=rng.normal(0, sigma, (hidden,)).astype(np.float16), shared_kinds=sk)
     return out
+
+
+# ---- configuration 3's routes: a prefill chunk's top-10 of 512 experts, Zipf-skewed
+
+PREFILL_TOKENS, PREFILL_EXPERTS, PREFILL_TOP_K, ZIPF_S = 2048, 512, 10, 0.8
+
+
+def prefill_routes(tokens: int = PREFILL_TOKENS, experts: int = PREFILL_EXPERTS, k: int = PREFILL_TOP_K,
+                   s: float = ZIPF_S, seed: int = 2048) -> np.ndarray:
+    """(tokens, k) int32 expert ids: the top-k of logits N(0, 1) - s ln(rank_e), the ranks a seeded permutation of the
+    experts. s = 0.8 uses 364 of 512 experts at 2,048 tokens, as many as strata-mlx reports for its real layers
+    (340-395); at s = 1 only ~220 are used."""
+    rng = np.random.default_rng(seed)
+    logits = rng.standard_normal((tokens, experts)) - s * np.log(rng.permutation(experts) + 1)
+    return np.argsort(-logits, axis=1, kind="stable")[:, :k].astype(np.int32)

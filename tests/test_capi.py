@@ -90,3 +90,36 @@ def test_which_kernel_takes_a_tile_product():
     assert lib.sc_tile_matmul_path(k, 512, 64, 2048, 2, 32768, aligned, aligned) == 0  # rows not by 128
     assert lib.sc_tile_matmul_path(k, 512, 512, 2048, 2, 16 * 5000, aligned, aligned) == 0  # too many tiles
     assert lib.sc_tile_matmul_path(k, 512, 512, 2048, 2, 32768, ctypes.c_void_p((1 << 20) + 8), aligned) == 0
+
+
+def _decode_layer(base: int, shift: dict) -> "_lib.SCLayer":
+    """A decode block of the benchmark's shapes over fake, never dereferenced addresses; `shift` moves named
+    pointers off their 16-byte boundary."""
+    L = _lib.SCLayer()
+    L.hidden, L.inter, L.experts, L.top_k, L.shared_inter = 2048, 512, 512, 10, 512
+    L.kind_gate = L.kind_up = L.kind_down = L.kind_sgate = L.kind_sup = L.kind_sdown = _lib.KINDS["Q2_0"]
+    for i, name in enumerate(("gate", "up", "down", "router", "sgate", "sup", "sdown", "shared_gate")):
+        setattr(L, name, base + (i << 24) + shift.get(name, 0))
+    L.dtype = _lib.DTYPES[torch.bfloat16]
+    return L
+
+
+def test_the_decode_block_refuses_pointers_off_16_bytes_before_any_launch():
+    """The fused kernels bulk-copy expert rows and read router rows and the window 16 bytes at a time: a pointer at
+    an odd offset is refused with SC_ERR_ALIGN on the host, before anything is enqueued (no GPU is used here)."""
+    lib = _lib.load()
+    base, x = 1 << 32, (1 << 32) - (1 << 24)
+    ws = ctypes.c_void_p(1 << 30)
+    for name in ("router", "shared_gate"):  # every path reads these 16 bytes at a time
+        L = _decode_layer(base, {name: 2})
+        n = lib.sc_moe_decode_workspace(ctypes.addressof(L), 1)
+        assert n > 0  # the size does not depend on the pointers
+        assert lib.sc_moe_decode_layer(ctypes.addressof(L), x, 1, x, ws, n, None) == -4, name
+    for name in ("gate", "up", "down", "sgate", "sup", "sdown"):  # the fused kernels' bulk copies
+        L = _decode_layer(base, {name: 8})
+        n = lib.sc_moe_decode_workspace(ctypes.addressof(L), 1)
+        assert lib.sc_moe_decode_stage(ctypes.addressof(L), x, 1, x, ws, n, 1, None) == -4, name
+        assert lib.sc_moe_decode_layer_ep(ctypes.addressof(L), x, 1, 0, 256, x, ws, n, None) == -4, name
+    L = _decode_layer(base, {})
+    n = lib.sc_moe_decode_workspace(ctypes.addressof(L), 1)
+    assert lib.sc_moe_decode_stage(ctypes.addressof(L), x + 4, 1, x, ws, n, 1, None) == -4  # the window

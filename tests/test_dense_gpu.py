@@ -194,3 +194,45 @@ def test_an_embedding_of_blocks_gives_the_rows_of_the_weights(cuda, kind, dtype)
     one = emb(torch.tensor([4], device="cuda"))
     assert one.shape == (1, t.shape[1])
     assert torch.equal(one, emb(torch.tensor([[4]], device="cuda"))[0])
+
+
+# Q8_0 dense tensors (strata_mlx/gguf.py:203-206: a weight is d * int8 code, blocks of 32) -- the attention
+# projections of the long-context configuration -- through the window kernel and BlockLinear.
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("tokens", [1, 2, 5, 8])
+def test_q8_0_window_products_are_the_weights_products(cuda, tokens, dtype):
+    from strata_mlx_b200.blocks import window_matvec
+
+    rows, cols = 1024, 2048
+    t = random_tensor("Q8_0", seed=80 + tokens, shape=(rows, cols))
+    x = randn((tokens, cols), dtype, tokens)
+    got = window_matvec(torch.from_numpy(t.data).cuda(), "Q8_0", rows, cols, x)
+    torch.cuda.synchronize()
+    from strata_mlx_b200 import _lib
+
+    _lib.check_device_errors()
+    want = x.float().cpu().numpy().astype(np.float64) @ weights(t).astype(np.float64).T
+    assert got.shape == (tokens, rows) and got.dtype == dtype
+    err = np.abs(got.float().cpu().numpy() - want).max() / np.abs(want).max()
+    assert err <= (1e-5 if dtype == torch.float32 else 2e-3 if dtype == torch.float16 else 8e-3), err
+
+
+@pytest.mark.parametrize("tokens", [1, 3, MAX_TOKENS + 4])
+def test_a_q8_0_layer_of_blocks_multiplies_as_its_weights_do(cuda, tokens):
+    t = random_tensor("Q8_0", seed=8, shape=(256, 1024))
+    lin = linear(t, as_blocks=("Q8_0",))
+    assert isinstance(lin, BlockLinear) and lin.nbytes == t.data.nbytes
+    x = randn((tokens, t.shape[1]), torch.float32, tokens)
+    want = x.cpu().numpy().astype(np.float64) @ weights(t).astype(np.float64).T
+    assert np.abs(lin(x).cpu().numpy() - want).max() <= 2e-5 * np.abs(want).max()
+
+
+def test_a_q8_0_window_gives_each_token_what_it_gets_alone(cuda):
+    t = random_tensor("Q8_0", seed=5, shape=(512, 1024))
+    lin = linear(t, as_blocks=("Q8_0",))
+    x = randn((6, t.shape[1]), torch.bfloat16, 6)
+    together = lin(x)
+    for i in range(6):
+        assert torch.equal(lin(x[i : i + 1]), together[i : i + 1])

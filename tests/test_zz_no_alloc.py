@@ -46,8 +46,10 @@ def test_the_block_without_a_workspace_gives_the_bits_of_the_block_with_one(cuda
         got = torch.full_like(x, float("nan"))
         rc = lib.sc_moe_decode_layer_noalloc(ctypes.addressof(layer.layer), x.data_ptr(), tokens, got.data_ptr(), stream)
         assert rc == 0, lib.sc_error_string(rc).decode()
-        torch.cuda.synchronize()
-        _lib.check_device_errors()
+        code = ctypes.c_int(-1)
+        assert lib.sc_moe_decode_noalloc_error(ctypes.byref(code), stream) == 0
+        assert code.value == 0, f"call {call}: its kernels recorded {_lib.ERRORS.get(code.value, code.value)}"
+        layer.check_errors()
         assert torch.equal(got, want), f"call {call}: the two entry points differ"
         ref, _, _ = R.moe_layer(x.float().cpu().numpy(), L["router"], L["shared_gate"], W["gate"], W["up"], W["down"],
                                 W["sgate"], W["sup"], W["sdown"], K, "bfloat16")
