@@ -201,6 +201,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// A failed CUDA call in host code: SC_ERR_CUDA, and with SC_VERBOSE=1 in the environment the call site and CUDA's
+// error name on stderr (the C ABI returns codes only; this is for finding which call failed).
+int cuda_failed(cudaError_t e, const char* where);
+
+// Raises kernel `kern`'s dynamic shared-memory limit on the current device to at least `bytes`, remembering per
+// (device, kernel) what it was set to, so that the driver is called only when a launch needs more than before.
+// The record is per kernel: several host paths that launch one kernel with different sizes share it.
+int raise_smem(const void* kern, int bytes, const char* where);
+
 __host__ __device__ constexpr int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ constexpr int align16(int v) { return (v + 15) & ~15; }
 

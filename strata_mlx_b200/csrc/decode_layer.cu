@@ -805,23 +805,19 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
                        : route_kernel<T, MAXT>;
   auto kg = gate_up_kernel<KGU, T>;
   auto kd = down_kernel<KD, T>;
-  // the dynamic shared memory a launch may take is raised to what it needs (the opt-in limit counts the kernel's
-  // static shared memory too), once per function and size
-  static int gu_set = 48 * 1024, dn_set = 48 * 1024;
-  if (gu_total > gu_set) {
-    if (cudaFuncSetAttribute(kg, cudaFuncAttributeMaxDynamicSharedMemorySize, gu_total) != cudaSuccess) return SC_ERR_CUDA;
-    gu_set = gu_total;
-  }
-  if (dn_total > dn_set) {
-    if (cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, dn_total) != cudaSuccess) return SC_ERR_CUDA;
-    dn_set = dn_total;
-  }
+  // the dynamic shared memory a launch may take is raised to what it needs, per kernel: the gate/up and down
+  // kernels are shared by the paths of several block-type mixes, each with its own sizes
+  if (int rc = raise_smem(reinterpret_cast<const void*>(kg), gu_total, "decode gate_up smem attribute")) return rc;
+  if (int rc = raise_smem(reinterpret_cast<const void*>(kd), dn_total, "decode down smem attribute")) return rc;
   const int grid_r = int(ceil_div(L.E + 1, RT_WARPS));
   const int grid_g = max_units * int(ceil_div(std::max(L.I, L.Is), RG));
   const int grid_d = L.H / RC;
-  if ((stage < 0 || stage == 0) && launch_pdl(kr, grid_r, RT_THREADS, 0, s, L) != cudaSuccess) return SC_ERR_CUDA;
-  if ((stage < 0 || stage == 1) && launch_pdl(kg, grid_g, WARPS * 32, gu_total, s, L) != cudaSuccess) return SC_ERR_CUDA;
-  if ((stage < 0 || stage == 2) && launch_pdl(kd, grid_d, DN_THREADS, dn_total, s, L) != cudaSuccess) return SC_ERR_CUDA;
+  if (stage < 0 || stage == 0)
+    if (cudaError_t e = launch_pdl(kr, grid_r, RT_THREADS, 0, s, L)) return cuda_failed(e, "decode route launch");
+  if (stage < 0 || stage == 1)
+    if (cudaError_t e = launch_pdl(kg, grid_g, WARPS * 32, gu_total, s, L)) return cuda_failed(e, "decode gate_up launch");
+  if (stage < 0 || stage == 2)
+    if (cudaError_t e = launch_pdl(kd, grid_d, DN_THREADS, dn_total, s, L)) return cuda_failed(e, "decode down launch");
   return SC_OK;
 }
 

@@ -1,5 +1,37 @@
 // Version, error strings and block-type sizes of the C ABI.
+#include <cstdio>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
+
+namespace sc {
+int cuda_failed(cudaError_t e, const char* where) {
+  static const bool verbose = [] {
+    const char* v = std::getenv("SC_VERBOSE");
+    return v && v[0] == '1';
+  }();
+  if (verbose) std::fprintf(stderr, "strata_cuda: %s: %s (%s)\n", where, cudaGetErrorName(e), cudaGetErrorString(e));
+  return SC_ERR_CUDA;
+}
+
+int raise_smem(const void* kern, int bytes, const char* where) {
+  static std::mutex lock;
+  static std::map<std::pair<int, const void*>, int> set;
+  if (bytes <= 48 * 1024) return SC_OK;  // every kernel takes this much without asking
+  int device = 0;
+  if (cudaError_t e = cudaGetDevice(&device)) return cuda_failed(e, where);
+  std::lock_guard<std::mutex> hold(lock);
+  int& now = set[{device, kern}];
+  if (bytes <= now) return SC_OK;
+  if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))
+    return cuda_failed(e, where);
+  now = bytes;
+  return SC_OK;
+}
+}  // namespace sc
 
 using namespace sc;
 
