@@ -21,6 +21,7 @@
 #include "mma_decode.cuh"
 #include "route.cuh"
 #include "decode_layer.cuh"
+#include "decode_dev.cuh"
 #include "ep.cuh"
 
 namespace sc {
@@ -72,74 +73,11 @@ __device__ unsigned long long g_trace[3][8192][8];
   } while (0)
 #endif
 
-__device__ __forceinline__ void named_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-template <typename T>
-__device__ __forceinline__ float dot8_half(const uint4& w, const uint4& x) {
-  const __half2* wh = reinterpret_cast<const __half2*>(&w);
-  const T* xv = reinterpret_cast<const T*>(&x);
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __half22float2(wh[j]);
-    s = fmaf(f.x, to_f32(xv[2 * j]), s);
-    s = fmaf(f.y, to_f32(xv[2 * j + 1]), s);
-  }
-  return s;
-}
-
 // ---------------------------------------------------------------------------------------------------- route
-
-// A float as an unsigned key in the same order (larger float, larger key)
-__device__ __forceinline__ uint32_t fkey(float v) {
-  const uint32_t u = __float_as_uint(v);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float unkey(uint32_t k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k); }
-
-// One round of a warp's selection: the largest key among the lanes' candidates, ties to the lower index; two
-// warp reductions (redux.sync). Returns the winner's index (0xffffffff when no lane has a candidate).
-__device__ __forceinline__ uint32_t warp_best(uint32_t key, uint32_t idx, uint32_t& best_key) {
-  best_key = __reduce_max_sync(0xffffffffu, key);
-  return __reduce_min_sync(0xffffffffu, key == best_key ? idx : 0xffffffffu);
-}
-
-// The k largest of a lane-held set: lane l holds keys kv[i] with indices iv[i] (i < PER; index 0xffffffff for none).
-// Writes keys and indices largest first (ties to the lower index) through lane 0.
-template <int PER>
-__device__ __forceinline__ void warp_select(uint32_t (&kv)[PER], uint32_t (&iv)[PER], int k, int lane, uint32_t* out_k,
-                                            uint32_t* out_i) {
-  for (int r = 0; r < k; ++r) {
-    uint32_t bk = 0, bi = 0xffffffffu;
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      if (iv[i] != 0xffffffffu && (bi == 0xffffffffu || kv[i] > bk || (kv[i] == bk && iv[i] < bi))) {
-        bk = kv[i];
-        bi = iv[i];
-      }
-    uint32_t top;
-    const uint32_t who = warp_best(bi == 0xffffffffu ? 0u : bk, bi, top);
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      if (iv[i] == who) iv[i] = 0xffffffffu;  // indices are distinct: only the winner's slot matches
-    if (lane == 0) {
-      out_k[r] = top;
-      out_i[r] = who;
-    }
-  }
-}
-
-__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // MT: the tokens the last block's registers are laid out for (1, 2, 4 or MAXT, the window's tokens or more: a shorter
 // tail for small windows, as expert parallel makes them: one token a rank)
@@ -200,195 +138,19 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   pdl_launch_dependents();
   TRACE_POINT(0, 3);
 
-  // ---- the last block: top-k of each token. Every step is a few dependent operations across all lanes: a long
-  // chain of dependent shuffles or selection rounds in one warp costs microseconds here.
-  // A. warp w takes the logits [seg w, seg w + seg) (seg 32 or 64, one or two a lane) and their maximum;
-  // B. theta = the K-th largest of the warps' maxima (0 when fewer than K warps hold logits): K warps each hold a
-  //    logit >= theta, so every logit of the top K is >= theta;
-  // C. the logits >= theta (usually a few more than K) are gathered into a short list;
-  // D. warp t ranks token t's list by broadcast reads of it, keeps the K best in order (ties to the lower index,
-  //    as the reference's argpartition + sort) and takes their softmax. A list longer than CAP (many ties) falls
-  //    back to K rounds of selection over all the logits.
-  constexpr int CAP = 128;
-  constexpr uint32_t NONE = 0xffffffffu;
-  __shared__ uint32_t w_max[MAXT][RT_WARPS], s_theta[MAXT], s_cnt[MAXT];
-  __shared__ __align__(16) uint32_t m_k[MAXT][CAP], m_i[MAXT][CAP];
-  __shared__ uint32_t s_key[MAXT * TOPK_MAX_K], s_idx[MAXT * TOPK_MAX_K];
-  __shared__ float s_w[MAXT * TOPK_MAX_K];
-  __shared__ uint32_t s_bits[32], s_pre[32], s_mask[MAXU], s_kpack[MAXU];
-  __shared__ int s_expert[MAXU];
-  const int seg = E > RT_WARPS * 32 ? 64 : 32;
-  const int live = int(ceil_div(E, seg));  // warps with logits
-  const int base = seg * warp;
-  const bool ok0 = warp < live && base + lane < E, ok1 = warp < live && seg == 64 && base + 32 + lane < E;
-  uint32_t k0[MT], k1[MT];  // keys of invalid slots are 0, below every non-NaN logit's key
-#pragma unroll
-  for (int t = 0; t < MT; ++t) {
-    k0[t] = ok0 && t < T_ ? fkey(__ldcg(L.logits + int64_t(t) * E + base + lane)) : 0u;
-    k1[t] = ok1 && t < T_ ? fkey(__ldcg(L.logits + int64_t(t) * E + base + 32 + lane)) : 0u;
-  }
-  TRACE_WARP(0, 0);
-#pragma unroll
-  for (int t = 0; t < MT; ++t) {
-    const uint32_t mx = __reduce_max_sync(0xffffffffu, max(k0[t], k1[t]));
-    if (lane == 0 && t < T_) w_max[t][warp] = mx;
-  }
-  if (tid < MAXT) s_cnt[tid] = 0;
-  for (int i = tid; i < 32; i += blockDim.x) s_bits[i] = 0;
-  for (int u = tid; u < MAXU; u += blockDim.x) {
-    s_mask[u] = 0;
-    s_kpack[u] = 0;
-  }
-  __syncthreads();
-  if (warp < T_) {  // B, warp t for token t: lane l < live ranks warp l's maximum among the live warps' maxima
-    const int t = warp;
-    const uint32_t v = lane < live ? w_max[t][lane] : 0u;
-    int r = 0;
-#pragma unroll
-    for (int j = 0; j < RT_WARPS; ++j) {
-      const uint32_t a = j < live ? w_max[t][j] : 0u;
-      r += int(a > v) | (int(a == v) & int(j < lane));
-    }
-    const uint32_t th = __reduce_max_sync(0xffffffffu, lane < live && r == K - 1 ? v : 0u);
-    if (lane == 0) s_theta[t] = th;
-  }
-  __syncthreads();
-  TRACE_WARP(0, 1);
-#pragma unroll
-  for (int t = 0; t < MT; ++t) {  // C
-    if (t >= T_) break;
-    const uint32_t th = s_theta[t];
-    const bool in0 = ok0 && k0[t] >= th, in1 = ok1 && k1[t] >= th;
-    const uint32_t b0 = __ballot_sync(0xffffffffu, in0), b1 = __ballot_sync(0xffffffffu, in1);
-    if (b0 | b1) {
-      int at = 0;
-      if (lane == 0) at = atomicAdd(&s_cnt[t], __popc(b0) + __popc(b1));
-      at = __shfl_sync(0xffffffffu, at, 0);
-      const int p0 = at + __popc(b0 & ((1u << lane) - 1u)), p1 = at + __popc(b0) + __popc(b1 & ((1u << lane) - 1u));
-      if (in0 && p0 < CAP) {
-        m_k[t][p0] = k0[t];
-        m_i[t][p0] = uint32_t(base + lane);
-      }
-      if (in1 && p1 < CAP) {
-        m_k[t][p1] = k1[t];
-        m_i[t][p1] = uint32_t(base + 32 + lane);
-      }
-    }
-  }
-  __syncthreads();
-  TRACE_POINT(0, 6);
-  for (int t = warp; t < T_; t += RT_WARPS) {  // D
-    const int m = int(s_cnt[t]);
-    TRACE_WARP(0, 2);
-    if (m <= CAP) {
-      // lane l ranks entries l, l + 32, ... of the list; four partial counts keep the chains short
-      const int nq = (m + 31) / 32;
-#pragma unroll
-      for (int q = 0; q < CAP / 32; ++q) {
-        if (q >= nq) break;
-        const bool in = lane + 32 * q < m;
-        const uint32_t kc = in ? m_k[t][lane + 32 * q] : 0u, ic = in ? m_i[t][lane + 32 * q] : NONE;
-        TRACE_WARP(0, 3);
-#ifdef SC_TRACE
-        const long long c0_ = clock64();
-#endif
-        int r4[4] = {0, 0, 0, 0};
-        for (int j = 0; j < m; j += 4) {  // entries past m hold stale values: masked by j + e < m
-          const uint4 a = *reinterpret_cast<const uint4*>(&m_k[t][j]);
-          const uint4 ai = *reinterpret_cast<const uint4*>(&m_i[t][j]);
-          const uint32_t av[4] = {a.x, a.y, a.z, a.w}, aiv[4] = {ai.x, ai.y, ai.z, ai.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e)  // bitwise, not && / ||: no branches in the chain
-            r4[e] += int(j + e < m) & (int(av[e] > kc) | (int(av[e] == kc) & int(aiv[e] < ic)));
-        }
-        const int r = r4[0] + r4[1] + r4[2] + r4[3];
-#ifdef SC_TRACE
-        const long long c1_ = clock64();
-        if (lane == 0) {
-          g_trace[0][4300 + t][0] = (unsigned long long)(c1_ - c0_);
-          g_trace[0][4300 + t][1] = (unsigned long long)m;
-          g_trace[0][4300 + t][2] = (unsigned long long)r;
-        }
-#endif
-        if (in && r < K) {
-          s_key[t * K + r] = kc;
-          s_idx[t * K + r] = ic;
-        }
-      }
-    } else {
-      // K rounds over all the logits, each taking the best that comes after the previous pick in the order
-      uint32_t pk = 0, pi = NONE;
-      for (int rr = 0; rr < K; ++rr) {
-        uint32_t bk = 0, bi = NONE;
-        for (int j = lane; j < E; j += 32) {
-          const uint32_t kj = fkey(__ldcg(L.logits + int64_t(t) * E + j));
-          const bool after = pi == NONE || kj < pk || (kj == pk && uint32_t(j) > pi);
-          if (after && (bi == NONE || kj > bk)) {  // j ascends: an equal key keeps the lower index
-            bk = kj;
-            bi = uint32_t(j);
-          }
-        }
-        const uint32_t who = warp_best(bi == NONE ? 0u : bk, bi, pk);
-        pi = who;
-        if (lane == 0) {
-          s_key[t * K + rr] = pk;
-          s_idx[t * K + rr] = who;
-        }
-      }
-    }
-    __syncwarp();
-    TRACE_WARP(0, 4);
-    // softmax over the chosen logits (fused.py:491), lane k taking choice k
-    const float top = unkey(s_key[t * K]);
-    const float e = lane < K ? expf(unkey(s_key[t * K + lane]) - top) : 0.f;
-    float sum = e;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane < K) s_w[t * K + lane] = e / sum;
-    TRACE_WARP(0, 5);
-#ifdef SC_TRACE
-    if (lane == 0) g_trace[0][4200 + t][0] = uint32_t(m);
-#endif
-  }
-  __syncthreads();
+  // ---- the last block: top-k of each token, the softmax and the plan (decode_dev.cuh)
+  __shared__ TailSmem S;
+  const int units = route_tail<MT>(L.logits, T_, E, K, L.e0, L.e1, S, tid, [] { __syncthreads(); });
   TRACE_POINT(0, 4);
-  const int P = T_ * K;
-  for (int p = tid; p < P; p += blockDim.x) {  // this rank's distinct experts as bits of a bitmap (E <= 1024)
-    L.idx[p] = s_idx[p];
-    L.wts[p] = s_w[p];
-    const int le = int(s_idx[p]) - L.e0;  // the local expert
-    if (le >= 0 && int(s_idx[p]) < L.e1) atomicOr(&s_bits[le >> 5], 1u << (le & 31));
+  for (int p = tid; p < T_ * K; p += blockDim.x) {
+    L.idx[p] = S.s_idx[p];
+    L.wts[p] = S.s_w[p];
   }
-  __syncthreads();
-  if (warp == 0) {  // exclusive prefix of the bitmap's popcounts
-    const int c = __popc(s_bits[lane]);
-    int incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    s_pre[lane] = uint32_t(incl - c);
-  }
-  __syncthreads();
-  for (int p = tid; p < P; p += blockDim.x) {
-    const int le = int(s_idx[p]) - L.e0;
-    if (le < 0 || int(s_idx[p]) >= L.e1) continue;  // another rank's expert
-    const uint32_t e = uint32_t(le);
-    // unit 0 is the shared expert; the routed units follow in ascending expert order
-    const int u = 1 + int(s_pre[e >> 5]) + __popc(s_bits[e >> 5] & ((1u << (e & 31)) - 1u));
-    const int tok = p / K, k = p % K;
-    s_expert[u] = int(e);
-    atomicOr(&s_mask[u], 1u << tok);
-    atomicOr(&s_kpack[u], uint32_t(k) << (4 * tok));
-  }
-  __syncthreads();
-  const int units = 1 + int(s_pre[31]) + __popc(s_bits[31]);
   for (int u = tid; u < units; u += blockDim.x) {
     Unit v;
-    v.expert = u == 0 ? -1 : s_expert[u];
-    v.tokmask = u == 0 ? (L.Is > 0 ? (1u << T_) - 1u : 0u) : s_mask[u];
-    v.kpack = u == 0 ? 0u : s_kpack[u];
+    v.expert = u == 0 ? -1 : S.s_expert[u];
+    v.tokmask = u == 0 ? (L.Is > 0 ? (1u << T_) - 1u : 0u) : S.s_mask[u];
+    v.kpack = u == 0 ? 0u : S.s_kpack[u];
     v.pad = 0;
     L.plan->unit[u] = v;
   }
