@@ -204,6 +204,23 @@ SC_API size_t sc_moe_decode_workspace(const sc_moe_layer* layer, int tokens);
 /* Offsets in the workspace of the last call's routes: idx (tokens, K) uint32 and weights (tokens, K) float32. */
 SC_API int sc_moe_decode_routes(const sc_moe_layer* layer, int tokens, size_t* idx_offset, size_t* weight_offset);
 
+/* A chain of decode blocks in one launch (no counterpart in strata-mlx, whose engine calls _Routed.__call__ once per
+ * layer, strata_mlx/engine.py:276-279): layers[0 .. n_layers) applied in turn to a window of `tokens` (1..8) tokens,
+ * each layer taking the previous one's output, except that every `refeed`-th layer (refeed > 0) takes x again; out
+ * (tokens, H) is the last layer's output. Every layer has the same shape and activation type and is one that
+ * sc_moe_decode_layer's fused path takes; n_layers <= 64; hidden a multiple of 128. One persistent kernel, a block
+ * an SM (a cooperative launch): per layer the router, a grid-wide barrier, the routes (every block), the gate/up
+ * products, a barrier, the down products, and the combine; the same bits as sc_moe_decode_layer layer by layer.
+ * workspace: sc_moe_decode_chain_workspace bytes, zeroed before its first use (its first words are the error word
+ * and the kernel's barrier count, which each launch leaves at zero); after a launch whose kernel recorded an error
+ * in the error word, zero it again. Each layer's routes stay readable: sc_moe_decode_chain_routes gives the offsets
+ * of idx (n_layers, tokens, K) uint32 and weights (n_layers, tokens, K) float32. */
+SC_API int sc_moe_decode_chain(const sc_moe_layer* layers, int n_layers, const void* x, int tokens, int refeed,
+                               void* out, void* workspace, size_t workspace_bytes, void* stream);
+SC_API size_t sc_moe_decode_chain_workspace(const sc_moe_layer* layers, int n_layers, int tokens);
+SC_API int sc_moe_decode_chain_routes(const sc_moe_layer* layers, int n_layers, int tokens, size_t* idx_offset,
+                                      size_t* weight_offset);
+
 /* One of the three kernels of sc_moe_decode_layer's fused path -- stage 0 routes (router, top-k, plan), 1 the
  * experts' gate/up, 2 the down products and the combine -- on a workspace that a previous sc_moe_decode_layer call
  * with the same layer and token count filled. For timing and profiling the kernels one at a time (no counterpart

@@ -237,6 +237,77 @@ class MoEDecodeLayer:
         return idx, w
 
 
+class DecodeChain:
+    """A stack of decode layers (MoEDecodeLayer, one shape) run by one launch of sc_moe_decode_chain: the persistent
+    kernel routes and multiplies every layer in turn, grid-wide barriers between its phases, so that no launch
+    separates the layers. __call__(x) applies the layers to the window x (tokens, hidden) -- each layer taking the
+    previous one's output, or x again every `refeed` layers -- and returns the last layer's output. The same bits as
+    calling the layers one by one."""
+
+    def __init__(self, layers: list, refeed: int = 0):
+        import ctypes
+
+        if not layers:
+            raise ValueError("a chain needs a layer")
+        self.layers, self.refeed = layers, refeed
+        self.hidden, self.dtype, self.top_k = layers[0].hidden, layers[0].dtype, layers[0].top_k
+        self._structs = (_lib.SCLayer * len(layers))(*[l.layer for l in layers])
+        self._ws: dict = {}
+        self._out: dict = {}
+
+    def _ref(self) -> int:
+        import ctypes
+
+        return ctypes.addressof(self._structs)
+
+    def workspace(self, tokens: int, device) -> torch.Tensor:
+        ws = self._ws.get((tokens, device))
+        if ws is None:
+            n = _lib.lib().sc_moe_decode_chain_workspace(self._ref(), len(self.layers), tokens)
+            if n == 0:
+                raise ValueError(f"sc_moe_decode_chain does not take these layers at {tokens} tokens")
+            ws = torch.zeros(n, dtype=torch.uint8, device=device)  # zeroed once: the kernel's barrier count
+            self._ws[(tokens, device)] = ws
+        return ws
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        require_cuda(x)
+        xs = x.reshape(-1, self.hidden)
+        if xs.dtype != self.dtype:
+            raise ValueError(f"activations of {xs.dtype}; the chain was built for {self.dtype}")
+        xs = xs if xs.is_contiguous() else xs.contiguous()
+        tokens = xs.shape[0]
+        ws = self.workspace(tokens, x.device)
+        if out is None:
+            out = torch.empty_like(xs)
+        check(_lib.lib().sc_moe_decode_chain(self._ref(), len(self.layers), ptr(xs), tokens, self.refeed, ptr(out),
+                                             ptr(ws), ws.numel(), stream()), "sc_moe_decode_chain")
+        return out.reshape(x.shape)
+
+    def routes(self, tokens: int, device) -> tuple:
+        """(idx (layers, tokens, K) uint32, weights (layers, tokens, K) float32) of the last call."""
+        import ctypes
+
+        io, wo = ctypes.c_size_t(), ctypes.c_size_t()
+        check(_lib.lib().sc_moe_decode_chain_routes(self._ref(), len(self.layers), tokens, ctypes.byref(io),
+                                                    ctypes.byref(wo)), "routes")
+        ws = self.workspace(tokens, device)
+        n, k = len(self.layers), self.top_k
+        idx = ws[io.value : io.value + n * tokens * k * 4].view(torch.int32).view(torch.uint32).reshape(n, tokens, k)
+        w = ws[wo.value : wo.value + n * tokens * k * 4].view(torch.float32).reshape(n, tokens, k)
+        return idx, w
+
+    def check_errors(self) -> None:
+        """Reads (synchronizing) the error words of the chain's workspaces; on an error zeroes the workspace (its
+        barrier count may be left mid-way) and raises."""
+        for ws in self._ws.values():
+            v = int(ws[:4].view(torch.int32).item())
+            if v:
+                ws.zero_()
+                raise _lib.StrataError(f"a kernel recorded {_lib.ERRORS.get(v, v)}: "
+                                       f"{_lib.lib().sc_error_string(v).decode()}")
+
+
 class DecodeGraph:
     """A stack of decode layers (MoEDecodeLayer) replayed as one CUDA graph: the call a serving loop makes per
     decoded window. __call__ takes the window's activations on the host (pinned, or any CPU tensor), copies them
@@ -246,8 +317,10 @@ class DecodeGraph:
     its MoE blocks and would otherwise grow without bound."""
 
     def __init__(self, layers: list, tokens: int, device=None, chain: bool = False, capture: bool = True,
-                 refeed: int = 0):
+                 refeed: int = 0, persistent: bool = False):
         self.layers, self.tokens, self.chain, self.capture, self.refeed = layers, tokens, chain, capture, refeed
+        # persistent: every layer in one launch of the chain kernel (DecodeChain); only the last output is kept
+        self.persistent = DecodeChain(layers, refeed if chain else 1) if persistent else None
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         H, dt = layers[0].hidden, layers[0].dtype
         self.x = torch.zeros((tokens, H), dtype=dt, device=dev)
@@ -256,6 +329,8 @@ class DecodeGraph:
         self.host_out = torch.zeros((tokens, H), dtype=dt).pin_memory()
         for l in layers:
             l.workspace(tokens, dev)
+        if self.persistent is not None:
+            self.persistent.workspace(tokens, dev)
         self.stream = torch.cuda.Stream(device=dev)
         self.graph = torch.cuda.CUDAGraph() if capture else None
         with torch.cuda.stream(self.stream):
@@ -266,6 +341,9 @@ class DecodeGraph:
                 self.run_layers()
 
     def run_layers(self) -> None:
+        if self.persistent is not None:
+            self.persistent(self.x, out=self.outs[-1])
+            return
         x = self.x
         for i, (l, o) in enumerate(zip(self.layers, self.outs)):
             if self.refeed and i % self.refeed == 0:
