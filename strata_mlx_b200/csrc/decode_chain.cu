@@ -27,7 +27,7 @@
 #include <algorithm>
 
 #include "matvec.cuh"
-#include "mma_decode.cuh"
+#include "frag_decode.cuh"
 #include "decode_layer.cuh"
 #include "decode_dev.cuh"
 
@@ -49,6 +49,21 @@ constexpr int DN_ROWS = GW * 16;         // output rows of a down item: a tile o
 constexpr int RG = 16;                   // gate/up rows of an item
 constexpr int CONS_BAR = 1;              // named barrier of the consumer threads; group g uses 2 + g
 constexpr long long WAIT_LIMIT = 2000000000LL;  // clock cycles: about a second
+
+// Phase stamps for a profiling build (-DSC_TRACE): %globaltimer per block, layer and phase. Compiled out otherwise.
+#ifdef SC_TRACE
+__device__ unsigned long long g_ctrace[160][MAXL][16];
+#define CK_TRACE(l, p)                                                               \
+  do {                                                                               \
+    unsigned long long t_;                                                           \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                           \
+    if (blockIdx.x < 160 && (l) < MAXL) g_ctrace[blockIdx.x][(l)][(p)] = t_;         \
+  } while (0)
+#else
+#define CK_TRACE(l, p) \
+  do {                 \
+  } while (0)
+#endif
 
 struct LayerW {
   const uint8_t *gate, *up, *down, *sgate, *sup, *sdown;
@@ -77,7 +92,7 @@ __host__ __device__ inline Smem smem_of(int T, int H, int rt_rows, int wmax, int
   Smem s;
   int o = 0;
   s.bars = o; o += 16 * 8;
-  s.tabs = o; o += align16(512 * 4 + 256 * 4 + 128);
+  s.tabs = o; o += align16(GRID_TAB_BYTES);
   s.x = o; o += align16(T * (H + 32) * 2);
   s.router = o; o += align16(rt_rows * H * 2);
   s.plan = o; o += align16(int(sizeof(dl::Plan)));
@@ -191,6 +206,7 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
   for (int l = 0; l < A.L && ok; ++l) {
     const LayerW& w = A.w[l];
     if (!(ok = mbar_wait(plan_ready, l & 1, A.err))) break;
+    CK_TRACE(l, 11);
     if (l + 1 < A.L) {
       if (!(ok = mbar_wait(rt_free, l & 1, A.err))) break;
       router(l + 1);
@@ -224,6 +240,7 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
       ++issued[s];
     }
     if (!ok) break;
+    CK_TRACE(l, 12);
     bool have_h = false;
     for (int j = I_.d0; j < I_.d1; ++j, ++it) {
       int u, c0;
@@ -241,11 +258,13 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
         if (!(ok = mbar_wait(hready, l & 1, A.err))) break;
         fence_proxy_async();  // h was written by other blocks' threads; the bulk copy reads it as the async proxy
         have_h = true;
+        CK_TRACE(l, 13);
       }
       bulk_load(dst + S.hoff, static_cast<const uint8_t*>(A.h) + size_t(u) * hbytes, hbytes, &full[s]);
       ++issued[s];
     }
     if (!ok) break;
+    CK_TRACE(l, 14);
     if (!have_h && !(ok = mbar_wait(hready, l & 1, A.err))) break;  // every phase of hready is waited once
     mbar_arrive(prod_done);
   }
@@ -254,66 +273,13 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
     if (issued[s]) mbar_wait(&full[s], (issued[s] - 1) & 1, A.err);
 }
 
-// ---- consumers: one gate/up item by a group of eight warps (the three-kernel block's gate_up_kernel arithmetic)
+// ---- consumers: a gate/up item is split over a group's eight warps by runs, four at a time (the three-kernel
+// block's gate_up_kernel split); a down item gives each warp a tile of 16 rows over every run (its down_piece)
 
-template <int KIND, typename T>
-__device__ __forceinline__ void gu_sums(const T* xs, int T_, int H, const uint8_t* wg, const uint8_t* wu, int64_t rb,
-                                        const uint32_t* grid, int w, int lane, float (&accg)[4], float (&accu)[4]) {
-  const int g = lane >> 2, t = lane & 3;
-  const int runs = H / 32, n0 = w * runs / GW, n1 = (w + 1) * runs / GW;
-  const uint8_t* ga = wg + g * rb;
-  const uint8_t* gb = wg + (g + 8) * rb;
-  const uint8_t* ua = wu + g * rb;
-  const uint8_t* ub = wu + (g + 8) * rb;
-#pragma unroll 4
-  for (int n = n0; n < n1; ++n) {
-    uint4 xv = make_uint4(0, 0, 0, 0);
-    if (g < T_) xv = *reinterpret_cast<const uint4*>(xs + g * (H + 32) + 32 * n + 8 * t);
-    uint32_t pa[4], pb[4];
-    {
-      const float sa = dec8<KIND, T>(ga, n, t, grid, pa), sb = dec8<KIND, T>(gb, n, t, grid, pb);
-      const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816<T>(d, a0, xv.x, xv.y);
-      mma16816<T>(d, a1, xv.z, xv.w);
-      accg[0] = fmaf(sa, d[0], accg[0]); accg[1] = fmaf(sa, d[1], accg[1]);
-      accg[2] = fmaf(sb, d[2], accg[2]); accg[3] = fmaf(sb, d[3], accg[3]);
-    }
-    {
-      const float sa = dec8<KIND, T>(ua, n, t, grid, pa), sb = dec8<KIND, T>(ub, n, t, grid, pb);
-      const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816<T>(d, a0, xv.x, xv.y);
-      mma16816<T>(d, a1, xv.z, xv.w);
-      accu[0] = fmaf(sa, d[0], accu[0]); accu[1] = fmaf(sa, d[1], accu[1]);
-      accu[2] = fmaf(sb, d[2], accu[2]); accu[3] = fmaf(sb, d[3], accu[3]);
-    }
-  }
-}
-
-// a warp's tile of a down item: rows st .. st + 16 of the unit's down product times its h (the three-kernel block's
-// down_piece arithmetic); acc the C fragment (rows g, g + 8; tokens 2t, 2t + 1)
-template <int KIND, typename T>
-__device__ __forceinline__ void dn_tile(const uint8_t* st, const T* hs, int hstride, int64_t rb, int cols, int T_,
-                                        uint32_t mask, const uint32_t* grid, int lane, float (&acc)[4]) {
-  const int g = lane >> 2, t = lane & 3;
-  const bool mine = g < T_ && ((mask >> g) & 1u);
-  const uint8_t* ra = st + g * rb;
-  const uint8_t* rbp = st + (g + 8) * rb;
-  acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-#pragma unroll 4
-  for (int n = 0; n < cols / 32; ++n) {
-    uint4 xv = make_uint4(0, 0, 0, 0);
-    if (mine) xv = *reinterpret_cast<const uint4*>(hs + g * hstride + 32 * n + 8 * t);
-    uint32_t pa[4], pb[4];
-    const float sa = dec8<KIND, T>(ra, n, t, grid, pa), sb = dec8<KIND, T>(rbp, n, t, grid, pb);
-    const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    mma16816<T>(d, a0, xv.x, xv.y);
-    mma16816<T>(d, a1, xv.z, xv.w);
-    acc[0] = fmaf(sa, d[0], acc[0]); acc[1] = fmaf(sa, d[1], acc[1]);
-    acc[2] = fmaf(sb, d[2], acc[2]); acc[3] = fmaf(sb, d[3], acc[3]);
-  }
+__device__ __forceinline__ void gu_runs(int H, int w, int& n0, int& n1) {
+  const int q4 = H / 128;
+  n0 = 4 * (w * q4 / GW);
+  n1 = 4 * ((w + 1) * q4 / GW);
 }
 
 template <typename F>
@@ -353,11 +319,8 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
     fence_mbar_init();
     s_abort = 0;
   }
-  {  // the codebooks of every kind a layer may have: IQ3_S's grid, IQ3_XXS's grid (Q2_0 needs none)
-    uint32_t* tb = reinterpret_cast<uint32_t*>(smem + S.tabs);
-    for (int i = tid; i < 512; i += THREADS) tb[i] = IQ3S_GRID[i];
-    for (int i = tid; i < 256; i += THREADS) tb[512 + i] = IQ3XXS_GRID[i];
-  }
+  // the codebooks of every kind a layer may have, expanded to four values of T an entry (Q2_0 needs none)
+  build_grid_tabs<T>(reinterpret_cast<uint2*>(smem + S.tabs), tid, THREADS);
   __syncthreads();
   if (warp == CW) {
     if (lane == 0) producer<T>(A, smem, S, r_lo, r_hi);
@@ -365,8 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
   }
 
   // ---- consumers
-  const uint32_t* grids[2] = {reinterpret_cast<const uint32_t*>(smem + S.tabs),
-                              reinterpret_cast<const uint32_t*>(smem + S.tabs) + 512};
+  const uint2* tabs = reinterpret_cast<const uint2*>(smem + S.tabs);
   T* xs = reinterpret_cast<T*>(smem + S.x);
   const uint8_t* rt = smem + S.router;
   dl::Plan* plan = reinterpret_cast<dl::Plan*>(smem + S.plan);
@@ -388,9 +350,12 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
     const int64_t rb_gu = row_bytes(w.kgu, H), rb_d = row_bytes(w.kd, A.I);
     const int64_t rb_sd = A.Is ? row_bytes(w.kd, A.Is) : 0;
     // ---- the window: the chain's input, or the previous layer's combined outputs
+    if (tid == 0) CK_TRACE(l, 0);
     const bool fresh = l == 0 || (A.refeed > 0 && l % A.refeed == 0);
-    stage_x_permuted<T>(static_cast<const T*>(fresh ? A.x : A.Xn), T_, H, xs, H + 32, tid, CT);
+    const bool pairs = x_pairs(w.kgu);
+    stage_x<T>(static_cast<const T*>(fresh ? A.x : A.Xn), T_, H, xs, H + 32, tid, CT, pairs);
     sync();
+    if (tid == 0) CK_TRACE(l, 1);
     // ---- R: this block's router rows
     if (!mbar_wait(rt_full, l & 1, A.err)) s_abort = 1;
     if (warp < r_hi - r_lo && s_abort == 0) {
@@ -400,9 +365,10 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
         const uint4* xr = reinterpret_cast<const uint4*>(xs + t * (H + 32)) + lane;
         float acc = 0.f;
         for (int c = 0; c < H / 256; ++c) {
-          const uint4 o = xr[32 * c];  // eight activations stored as (0,4) (1,5) (2,6) (3,7): back to 0..7
-          const uint4 v = make_uint4(__byte_perm(o.x, o.y, 0x5410), __byte_perm(o.z, o.w, 0x5410),
-                                     __byte_perm(o.x, o.y, 0x7632), __byte_perm(o.z, o.w, 0x7632));
+          const uint4 o = xr[32 * c];  // eight activations, stored as (0,4) (1,5) (2,6) (3,7) for a Q2_0 layer
+          const uint4 v = pairs ? make_uint4(__byte_perm(o.x, o.y, 0x5410), __byte_perm(o.z, o.w, 0x5410),
+                                             __byte_perm(o.x, o.y, 0x7632), __byte_perm(o.z, o.w, 0x7632))
+                                : o;
           acc += dl::dot8_half<T>(wv[32 * c], v);
         }
 #pragma unroll
@@ -414,8 +380,12 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       }
     }
     sync();
-    if (tid == 0) mbar_arrive(rt_free);
+    if (tid == 0) {
+      mbar_arrive(rt_free);
+      CK_TRACE(l, 2);
+    }
     if (!barrier()) return;  // A
+    if (tid == 0) CK_TRACE(l, 3);
     // ---- P: the window's routes and plan, in every block
     const int units = dl::route_tail<MT>(A.logits, T_, E, K, 0, E, TS, tid, sync);
     for (int u = tid; u < units; u += CT) {
@@ -440,7 +410,10 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
     }
     sync();
     if (s_abort) return;
-    if (tid == 0) mbar_arrive(plan_ready);
+    if (tid == 0) {
+      mbar_arrive(plan_ready);
+      CK_TRACE(l, 4);
+    }
     const Items I_ = items_of(units, A.I, A.Is, H, cta, G);
     // ---- G: gate/up items; item `it` goes to the group of its stage's parity
     for (int j = I_.g0; j < I_.g1; ++j, ++it) {
@@ -456,8 +429,13 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
       const bool got = mbar_wait(&full[s], (it / STAGES) & 1, A.err);
       if (got) {
+        int n0, n1;
+        gu_runs(H, gw, n0, n1);
+        const int g = lane >> 2;
+        const T* xg = g < T_ ? xs + g * (H + 32) : nullptr;
         by_kind(w.kgu, [&]<int KIND>() {
-          gu_sums<KIND, T>(xs, T_, H, wg, wu, rb, KIND == SC_IQ3_XXS ? grids[1] : grids[0], gw, lane, accg, accu);
+          frag_runs<KIND, T>(wg + g * rb, wg + (g + 8) * rb, xg, n0, n1, lane, grid_tab<KIND>(tabs), accg);
+          frag_runs<KIND, T>(wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane, grid_tab<KIND>(tabs), accu);
         });
       }
       __syncwarp();
@@ -483,16 +461,19 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
         }
         const int m = (q < 2 ? 0 : 8) + (Lq >> 2), tok = 2 * (Lq & 3) + (q & 1);
         if (tok < T_ && ((un.tokmask >> tok) & 1u)) {
-          // h in its consumer's fragment order (groups of eight as 0,4,1,5,2,6,3,7)
-          const int r = r0 + m, jj = r & 7, col = (r & ~7) + (jj < 4 ? 2 * jj : 2 * (jj - 4) + 1);
-          h[(int64_t(u) * T_ + tok) * A.hstride + col] = from_f32<T>(swiglu_mlx<T>(sg, su));
+          // h in the order its consumer (the down product's decoder) wants
+          h[(int64_t(u) * T_ + tok) * A.hstride + x_col(r0 + m, x_pairs(w.kd))] = from_f32<T>(swiglu_mlx<T>(sg, su));
         }
       }
       if (!got) s_abort = 1;
       named_sync(2 + grp, GW * 32);
     }
+    if (tid == 0) CK_TRACE(l, 5);
     if (!barrier()) return;  // B: every unit's h
-    if (tid == 0) mbar_arrive(hready);
+    if (tid == 0) {
+      mbar_arrive(hready);
+      CK_TRACE(l, 6);
+    }
     // ---- D: down items
     for (int j = I_.d0; j < I_.d1; ++j, ++it) {
       const int s = int(it % STAGES);
@@ -504,12 +485,15 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       const int64_t rb = sh ? rb_sd : rb_d;
       const uint8_t* st = stage0 + s * S.stage;
       const T* hs = reinterpret_cast<const T*>(st + S.hoff);
-      float acc[4];
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
       const bool got = mbar_wait(&full[s], (it / STAGES) & 1, A.err);
       if (got) {
+        const int g = lane >> 2;
+        const bool mine = g < T_ && ((un.tokmask >> g) & 1u);
+        const uint8_t* st0 = st + gw * 16 * rb;
         by_kind(w.kd, [&]<int KIND>() {
-          dn_tile<KIND, T>(st + gw * 16 * rb, hs, A.hstride, rb, sh ? A.Is : A.I, T_, un.tokmask,
-                           KIND == SC_IQ3_XXS ? grids[1] : grids[0], lane, acc);
+          frag_runs<KIND, T>(st0 + g * rb, st0 + (g + 8) * rb, mine ? hs + g * A.hstride : nullptr, 0,
+                             (sh ? A.Is : A.I) / 32, lane, grid_tab<KIND>(tabs), acc);
         });
       }
       __syncwarp();
@@ -530,8 +514,10 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
     }
     const bool last = l == A.L - 1;
     const bool next_fresh = !last && A.refeed > 0 && (l + 1) % A.refeed == 0;
+    if (tid == 0) CK_TRACE(l, 7);
     if (next_fresh) continue;  // the next layer takes the chain's input again: this layer's outputs are not needed
     if (!barrier()) return;  // C: every pair's output
+    if (tid == 0) CK_TRACE(l, 8);
     // ---- C: this block's slice of the window (moe_combine, fused.py:448-462), an output a thread
     const int n_out = T_ * H;
     const int q0 = int(int64_t(n_out) * cta / G), q1 = int(int64_t(n_out) * (cta + 1) / G);
@@ -546,8 +532,10 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       const float gv = A.Is > 0 ? round_to<T>(s_gsh[tok]) : -INFINITY;
       dst[q] = from_f32<T>(combine_one<T>(yk, s_wts + tok * K, K, gv, A.Is > 0 ? yk[K] : 0.f));
     }
+    if (tid == 0) CK_TRACE(l, 9);
     if (last) break;
     if (!barrier()) return;  // D: the next layer's window
+    if (tid == 0) CK_TRACE(l, 10);
   }
   // every block past the launch's last barrier: the last one resets the count for the next launch
   sync();
@@ -618,6 +606,12 @@ static int sm_count() {
 }  // namespace sc
 
 using namespace sc;
+
+#ifdef SC_TRACE
+extern "C" SC_API int sc_chain_trace_read(void* host) {
+  return cudaMemcpyFromSymbol(host, ck::g_ctrace, sizeof(ck::g_ctrace)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 extern "C" size_t sc_moe_decode_chain_workspace(const sc_moe_layer* layers, int n_layers, int tokens) {
   if (chain_check(layers, n_layers, tokens) != SC_OK) return 0;

@@ -18,7 +18,7 @@
 #include <algorithm>
 
 #include "matvec.cuh"
-#include "mma_decode.cuh"
+#include "frag_decode.cuh"
 #include "route.cuh"
 #include "decode_layer.cuh"
 #include "decode_dev.cuh"
@@ -174,7 +174,7 @@ __host__ __device__ inline GuSmem gu_smem(int tokens, int H, int64_t rb) {
   GuSmem s;
   int o = 0;
   s.bar = o; o += 16;
-  s.tabs = o; o += align16(2048 + 8);
+  s.tabs = o; o += align16(GRID_TAB_BYTES);
   s.xs = o; o += align16(tokens * (H + 32) * 2);
   s.red = o; o += WARPS * 32 * 8 * 4;
   s.rows = o; o += 2 * align16(int(RG * rb));
@@ -182,7 +182,7 @@ __host__ __device__ inline GuSmem gu_smem(int tokens, int H, int64_t rb) {
   return s;
 }
 
-template <int KIND, typename T>
+template <int KIND, int KD, typename T>
 __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   TRACE_POINT(1, 0);
   TRACE_SMID(1, 2);
@@ -213,16 +213,16 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
       bulk_load(wu, L.sup + r0 * rb, uint32_t(rows * rb), bar);
     }
   }
-  const uint32_t* grid = nullptr;
-  if constexpr (KIND == SC_IQ3_S) grid = load_tabs<KIND>(smem + S.tabs).iq3s;
-  if constexpr (KIND == SC_IQ3_XXS) grid = load_tabs<KIND>(smem + S.tabs).iq3xxs;
+  uint2* tabs = reinterpret_cast<uint2*>(smem + S.tabs);
+  if constexpr (KIND != SC_Q2_0) build_grid_tabs<T>(tabs, tid, blockDim.x);
+  const uint2* tab = grid_tab<KIND>(tabs);
   // the window's activations are complete once the route kernel let this kernel start (it waits before it does);
   // over peer memory, the window's count is read here too (already full), for the peers' writes' visibility
   if (L.peers) {
     if (tid == 0) ep::wait_count(ep::at_u32(L.peers[L.rank], ep::xcount_off(L.par)), L.xtarget, L.err);
     __syncthreads();
   }
-  stage_x_permuted<T>(static_cast<const T*>(L.x), T_, H, xs, H + 32, tid, blockDim.x);
+  stage_x<T>(static_cast<const T*>(L.x), T_, H, xs, H + 32, tid, blockDim.x, x_pairs(KIND));
   pdl_wait();  // the routes
   TRACE_POINT(1, 1);
   // only now may the down kernel start: it reads the routes and the plan before it waits on this kernel
@@ -245,39 +245,14 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   __syncthreads();
   if (u >= s_units) return;  // no such unit in this window (the grid is sized for the largest window)
 
-  const int g = lane >> 2, t = lane & 3;
-  const int runs = H / 32, n0 = warp * runs / WARPS, n1 = (warp + 1) * runs / WARPS;
-  const uint8_t* ga = wg + g * rb;
-  const uint8_t* gb = wg + (g + 8) * rb;
-  const uint8_t* ua = wu + g * rb;
-  const uint8_t* ub = wu + (g + 8) * rb;
+  const int g = lane >> 2;
+  const int q4 = H / 128, n0 = 4 * (warp * q4 / WARPS), n1 = 4 * ((warp + 1) * q4 / WARPS);  // runs, by fours
+  const T* xg = g < T_ ? xs + g * (H + 32) : nullptr;
   float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
   if (!mbar_wait(bar, 0, L.err)) return;
   TRACE_POINT(1, 3);
-#pragma unroll 4
-  for (int n = n0; n < n1; ++n) {
-    uint4 xv = make_uint4(0, 0, 0, 0);
-    if (g < T_) xv = *reinterpret_cast<const uint4*>(xs + g * (H + 32) + 32 * n + 8 * t);
-    uint32_t pa[4], pb[4];
-    {
-      const float sa = dec8<KIND, T>(ga, n, t, grid, pa), sb = dec8<KIND, T>(gb, n, t, grid, pb);
-      const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816<T>(d, a0, xv.x, xv.y);
-      mma16816<T>(d, a1, xv.z, xv.w);
-      accg[0] = fmaf(sa, d[0], accg[0]); accg[1] = fmaf(sa, d[1], accg[1]);
-      accg[2] = fmaf(sb, d[2], accg[2]); accg[3] = fmaf(sb, d[3], accg[3]);
-    }
-    {
-      const float sa = dec8<KIND, T>(ua, n, t, grid, pa), sb = dec8<KIND, T>(ub, n, t, grid, pb);
-      const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816<T>(d, a0, xv.x, xv.y);
-      mma16816<T>(d, a1, xv.z, xv.w);
-      accu[0] = fmaf(sa, d[0], accu[0]); accu[1] = fmaf(sa, d[1], accu[1]);
-      accu[2] = fmaf(sb, d[2], accu[2]); accu[3] = fmaf(sb, d[3], accu[3]);
-    }
-  }
+  frag_runs<KIND, T>(wg + g * rb, wg + (g + 8) * rb, xg, n0, n1, lane, tab, accg);
+  frag_runs<KIND, T>(wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane, tab, accu);
   TRACE_POINT(1, 4);
   // red[value][warp][lane]: the reducing thread (value q, lane L) reads eight consecutive words
   red[((0 + 0) * WARPS + warp) * 32 + lane] = accg[0];
@@ -299,9 +274,9 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
     }
     const int m = (q < 2 ? 0 : 8) + (Lq >> 2), tok = 2 * (Lq & 3) + (q & 1);
     if (m < rows && tok < T_ && ((s_unit.tokmask >> tok) & 1u)) {
-      // h is stored in its consumer's fragment order (groups of eight as 0,4,1,5,2,6,3,7)
-      const int r = r0 + m, j = r & 7, col = (r & ~7) + (j < 4 ? 2 * j : 2 * (j - 4) + 1);
-      static_cast<T*>(L.h)[(int64_t(u) * T_ + tok) * L.hstride + col] = from_f32<T>(swiglu_mlx<T>(sg, su));
+      // h is stored in the order its consumer (the down product's decoder) wants
+      static_cast<T*>(L.h)[(int64_t(u) * T_ + tok) * L.hstride + x_col(r0 + m, x_pairs(KD))] =
+          from_f32<T>(swiglu_mlx<T>(sg, su));
     }
   }
 }
@@ -319,7 +294,7 @@ __host__ __device__ inline DnSmem dn_smem(int tokens, int K, int stage_bytes, in
   DnSmem s;
   int o = 0;
   s.bars = o; o += align16(2 * MAX_STAGES * 8);
-  s.tabs = o; o += align16(2048 + 8);
+  s.tabs = o; o += align16(GRID_TAB_BYTES);
   s.plan = o; o += align16(int(sizeof(Plan)));
   s.wts = o; o += align16(tokens * (K + 1) * 4);
   s.ys = o; o += align16(tokens * (K + 1) * RC * 4);
@@ -333,8 +308,8 @@ __host__ __device__ inline DnSmem dn_smem(int tokens, int K, int stage_bytes, in
 // then the products. acc: the C fragment (rows g, g + 8; tokens 2t, 2t + 1).
 template <int KIND, typename T>
 __device__ __forceinline__ void down_piece(const LayerDev& L, uint8_t* st, int hoff, int u, int n0, int n1, bool shared,
-                                           uint32_t mask, const uint32_t* grid, int lane, float (&acc)[4]) {
-  const int T_ = L.T, g = lane >> 2, t = lane & 3;
+                                           uint32_t mask, const uint2* tab, int lane, float (&acc)[4]) {
+  const int T_ = L.T, g = lane >> 2;
   T* hs = reinterpret_cast<T*>(st + hoff);
   {
     const T* hu = static_cast<const T*>(L.h) + int64_t(u) * T_ * L.hstride;
@@ -357,22 +332,8 @@ __device__ __forceinline__ void down_piece(const LayerDev& L, uint8_t* st, int h
   }
   const int64_t rb = shared ? L.rb_sd : L.rb_d;
   const bool mine = g < T_ && ((mask >> g) & 1u);
-  const uint8_t* ra = st + g * rb;
-  const uint8_t* rbp = st + (g + 8) * rb;
   acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-#pragma unroll 4
-  for (int n = n0; n < n1; ++n) {
-    uint4 xv = make_uint4(0, 0, 0, 0);
-    if (mine) xv = *reinterpret_cast<const uint4*>(hs + g * L.hstride + 32 * n + 8 * t);
-    uint32_t pa[4], pb[4];
-    const float sa = dec8<KIND, T>(ra, n, t, grid, pa), sb = dec8<KIND, T>(rbp, n, t, grid, pb);
-    const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    mma16816<T>(d, a0, xv.x, xv.y);
-    mma16816<T>(d, a1, xv.z, xv.w);
-    acc[0] = fmaf(sa, d[0], acc[0]); acc[1] = fmaf(sa, d[1], acc[1]);
-    acc[2] = fmaf(sb, d[2], acc[2]); acc[3] = fmaf(sb, d[3], acc[3]);
-  }
+  frag_runs<KIND, T>(st + g * rb, st + (g + 8) * rb, mine ? hs + g * L.hstride : nullptr, n0, n1, lane, tab, acc);
 }
 
 template <int KIND, typename T>
@@ -399,9 +360,9 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
     }
     fence_mbar_init();
   }
-  const uint32_t* grid = nullptr;
-  if constexpr (KIND == SC_IQ3_S) grid = load_tabs<KIND>(smem + S.tabs).iq3s;
-  if constexpr (KIND == SC_IQ3_XXS) grid = load_tabs<KIND>(smem + S.tabs).iq3xxs;
+  uint2* tabs = reinterpret_cast<uint2*>(smem + S.tabs);
+  if constexpr (KIND != SC_Q2_0) build_grid_tabs<T>(tabs, tid, blockDim.x);
+  const uint2* tab = grid_tab<KIND>(tabs);
   // the routes and the plan are complete once the gate/up kernel let this kernel start (it waits before it does)
   for (int i = tid; i < int(sizeof(Plan) / 16); i += blockDim.x)
     reinterpret_cast<int4*>(plan)[i] = __ldcg(reinterpret_cast<const int4*>(L.plan) + i);
@@ -468,7 +429,7 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
       }
       const uint32_t mask = plan->unit[u].tokmask, kpack = plan->unit[u].kpack;
       float acc[4];
-      down_piece<KIND, T>(L, stage0 + s * L.dn_stage, hoff, u, 0, (shared ? L.Is : L.I) / 32, shared, mask, grid,
+      down_piece<KIND, T>(L, stage0 + s * L.dn_stage, hoff, u, 0, (shared ? L.Is : L.I) / 32, shared, mask, tab,
                           lane, acc);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -565,7 +526,7 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
             : L.T == 2 ? route_kernel<T, 2>
             : L.T <= 4 ? route_kernel<T, 4>
                        : route_kernel<T, MAXT>;
-  auto kg = gate_up_kernel<KGU, T>;
+  auto kg = gate_up_kernel<KGU, KD, T>;
   auto kd = down_kernel<KD, T>;
   // the dynamic shared memory a launch may take is raised to what it needs, per kernel: the gate/up and down
   // kernels are shared by the paths of several block-type mixes, each with its own sizes
@@ -606,7 +567,8 @@ bool v2_takes(const sc_moe_layer* L, int tokens) {
   if (L->shared_inter > 0 && (L->kind_sgate != L->kind_gate || L->kind_sup != L->kind_gate || L->kind_sdown != L->kind_down))
     return false;
   if (L->hidden % 256 || L->hidden / 256 > dl::MAX_ROUTER_CHUNKS || L->hidden % dl::RC) return false;
-  if (L->inter % 32 || L->inter % dl::RG || L->shared_inter % 32 || L->shared_inter % dl::RG) return false;
+  // the decoders take runs four at a time: rows of 128 weights
+  if (L->inter % 128 || L->shared_inter % 128) return false;
   if (row_bytes(L->kind_gate, L->hidden) % 16) return false;  // 16-row bulk copies start on 16 bytes
   return true;
 }
