@@ -623,7 +623,8 @@ def window_stream(layers, device, tokens: int = 8, reps: int = 20) -> dict:
     a layer carries enough bytes; one-token layers are latency-bound."""
     from strata_mlx_b200 import fused as F
 
-    g = F.DecodeGraph(layers, tokens=tokens, device=device, capture=True)
+    # every layer in one launch of the persistent chain kernel (each layer reads the window: refeed 1)
+    g = F.DecodeGraph(layers, tokens=tokens, device=device, capture=True, persistent=True)
     gen = torch.Generator(device=device)
     gen.manual_seed(8)
     xs = torch.randn((reps + 3, tokens, H), generator=gen, device=device).to(torch.bfloat16)
@@ -643,14 +644,16 @@ def window_stream(layers, device, tokens: int = 8, reps: int = 20) -> dict:
             e1.record(s)
         torch.cuda.synchronize()
         total_us += e0.elapsed_time(e1) * 1e3
-        for l in layers:  # the routes this step chose: the distinct experts each layer read
-            used = int(torch.unique(l.routes(tokens, device)[0].view(torch.int32)).numel())
+        routes = g.persistent.routes(tokens, device)[0]
+        for i, l in enumerate(layers):  # the routes this step chose: the distinct experts each layer read
+            used = int(torch.unique(routes[i].view(torch.int32)).numel())
             per_expert = 2 * I * row_bytes(l.kind, H) + H * row_bytes(l.kind, I)
             shared = 2 * IS * row_bytes(l.kind, H) + H * row_bytes(l.kind, IS)
             nbytes += used * per_expert + shared + E * H * 2
     us = total_us / reps
     nbytes /= reps
-    return {"api": "strata_mlx_b200.fused.DecodeGraph (48 layers, graph replay)", "tokens": tokens,
+    return {"api": "strata_mlx_b200.fused.DecodeGraph(persistent=True): sc_moe_decode_chain, 48 layers in one "
+                   "launch, graph replay", "tokens": tokens,
             "bytes_per_step": nbytes, "us_per_step": us, "gbs": nbytes / (us * 1e-6) / 1e9,
             "tok_per_s": tokens / (us * 1e-6)}
 

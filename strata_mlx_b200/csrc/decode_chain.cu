@@ -44,7 +44,7 @@ constexpr int GROUPS = 2;
 constexpr int CW = GW * GROUPS;          // consumer warps: the route tail's sixteen
 constexpr int CT = CW * 32;
 constexpr int THREADS = CT + 32;         // and the producer warp
-constexpr int STAGES = 4;                // two stages a group
+constexpr int MAX_STAGES = 8;            // a ring of an even number of stages: stage s is group s % 2's
 constexpr int DN_ROWS = GW * 16;         // output rows of a down item: a tile of 16 rows a warp
 constexpr int RG = 16;                   // gate/up rows of an item
 constexpr int CONS_BAR = 1;              // named barrier of the consumer threads; group g uses 2 + g
@@ -59,7 +59,18 @@ __device__ unsigned long long g_ctrace[160][MAXL][16];
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                           \
     if (blockIdx.x < 160 && (l) < MAXL) g_ctrace[blockIdx.x][(l)][(p)] = t_;         \
   } while (0)
+// per item of a layer (its index in the block's list, first 5): issued, data in, done
+__device__ unsigned long long g_itrace[160][MAXL][16];
+#define CK_ITRACE(l, i, p)                                                           \
+  do {                                                                               \
+    unsigned long long t_;                                                           \
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                           \
+    if (blockIdx.x < 160 && (l) < MAXL && (i) < 5) g_itrace[blockIdx.x][(l)][3 * (i) + (p)] = t_; \
+  } while (0)
 #else
+#define CK_ITRACE(l, i, p) \
+  do {                     \
+  } while (0)
 #define CK_TRACE(l, p) \
   do {                 \
   } while (0)
@@ -69,11 +80,12 @@ struct LayerW {
   const uint8_t *gate, *up, *down, *sgate, *sup, *sdown;
   const __half *router, *shared_gate;
   int kgu, kd;
+  int rb_gu, rb_d, rb_sd;  // bytes of a row: gate / up (and the shared expert's), down, the shared expert's down
 };
 
 struct Args {
   LayerW w[MAXL];
-  int L, T, H, I, Is, E, K, refeed, hstride, rt_rows, wmax;
+  int L, T, H, I, Is, E, K, refeed, hstride, rt_rows, wmax, stages;
   const void* x;
   void* out;
   int* err;
@@ -88,10 +100,10 @@ struct Smem {
   int bars, tabs, x, router, plan, routes, red, stages, stage, hoff, total;
 };
 
-__host__ __device__ inline Smem smem_of(int T, int H, int rt_rows, int wmax, int hstride) {
+__host__ __device__ inline Smem smem_of(int T, int H, int rt_rows, int wmax, int hstride, int stages) {
   Smem s;
   int o = 0;
-  s.bars = o; o += 16 * 8;
+  s.bars = o; o += (2 * MAX_STAGES + 8) * 8;
   s.tabs = o; o += align16(GRID_TAB_BYTES);
   s.x = o; o += align16(T * (H + 32) * 2);
   s.router = o; o += align16(rt_rows * H * 2);
@@ -101,7 +113,7 @@ __host__ __device__ inline Smem smem_of(int T, int H, int rt_rows, int wmax, int
   s.red = o; o += align16(red);
   s.hoff = align16(wmax);
   s.stage = s.hoff + align16(T * hstride * 2);
-  s.stages = align16(o); o = s.stages + STAGES * s.stage;
+  s.stages = align16(o); o = s.stages + stages * s.stage;
   s.total = o;
   return s;
 }
@@ -159,10 +171,10 @@ __device__ __forceinline__ Items items_of(int units, int I, int Is, int H, int c
   it.nd = H / DN_ROWS;
   const int ngu = it.nrbs + (units - 1) * it.nrb;
   const int ndn = (Is > 0 ? units : units - 1) * it.nd;
-  it.g0 = int(int64_t(ngu) * cta / G);
-  it.g1 = int(int64_t(ngu) * (cta + 1) / G);
-  it.d0 = int(int64_t(ndn) * cta / G);
-  it.d1 = int(int64_t(ndn) * (cta + 1) / G);
+  it.g0 = ngu * cta / G;
+  it.g1 = ngu * (cta + 1) / G;
+  it.d0 = ndn * cta / G;
+  it.d1 = ndn * (cta + 1) / G;
   return it;
 }
 
@@ -170,9 +182,10 @@ __device__ __forceinline__ Items items_of(int units, int I, int Is, int H, int c
 
 template <typename T>
 __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, int r_hi) {
+  const int STAGES = A.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S.bars);
-  uint64_t* empty = full + STAGES;
-  uint64_t* rt_full = empty + STAGES;
+  uint64_t* empty = full + MAX_STAGES;
+  uint64_t* rt_full = empty + MAX_STAGES;
   uint64_t* rt_free = rt_full + 1;
   uint64_t* plan_ready = rt_free + 1;
   uint64_t* hready = plan_ready + 1;
@@ -182,7 +195,7 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
   uint8_t* stage0 = smem + S.stages;
   const int H = A.H, E = A.E, T_ = A.T;
   const uint32_t hbytes = uint32_t(T_ * A.hstride * 2);
-  uint32_t issued[STAGES] = {0, 0, 0, 0};  // copies issued into each stage, for the drain at the end
+  uint32_t issued = 0;  // items issued, for the drain at the end
 
   auto router = [&](int l) {
     const LayerW& w = A.w[l];
@@ -211,12 +224,13 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
       if (!(ok = mbar_wait(rt_free, l & 1, A.err))) break;
       router(l + 1);
     }
+    CK_TRACE(l, 15);
+    const uint32_t it_layer = it;
     const int units = plan->units;
     const Items I_ = items_of(units, A.I, A.Is, H, blockIdx.x, gridDim.x);
-    const int64_t rb_gu = row_bytes(w.kgu, H), rb_d = row_bytes(w.kd, A.I);
-    const int64_t rb_sgu = A.Is ? row_bytes(w.kgu, H) : 0, rb_sd = A.Is ? row_bytes(w.kd, A.Is) : 0;
+    const int rb_gu = w.rb_gu, rb_d = w.rb_d, rb_sgu = w.rb_gu, rb_sd = w.rb_sd;
     auto slot = [&](int s) -> bool {
-      if (it >= STAGES && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, A.err)) return false;
+      if (it >= uint32_t(STAGES) && !mbar_wait(&empty[s], ((it / STAGES) - 1) & 1, A.err)) return false;
       return true;
     };
     for (int j = I_.g0; j < I_.g1; ++j, ++it) {
@@ -226,7 +240,7 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
       if (!(ok = slot(s))) break;
       uint8_t* dst = stage0 + s * S.stage;
       const bool sh = u == 0 && A.Is > 0;
-      const int64_t rb = sh ? rb_sgu : rb_gu;
+      const int rb = sh ? rb_sgu : rb_gu;
       const uint32_t bytes = uint32_t(RG * rb);
       mbar_arrive_expect_tx(&full[s], 2 * bytes);
       if (sh) {
@@ -237,7 +251,8 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
         bulk_load(dst, w.gate + (e * A.I + r0) * rb, bytes, &full[s]);
         bulk_load(dst + align16(int(bytes)), w.up + (e * A.I + r0) * rb, bytes, &full[s]);
       }
-      ++issued[s];
+      issued = it + 1;
+      CK_ITRACE(l, it - it_layer, 0);
     }
     if (!ok) break;
     CK_TRACE(l, 12);
@@ -249,7 +264,7 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
       if (!(ok = slot(s))) break;
       uint8_t* dst = stage0 + s * S.stage;
       const bool sh = u == 0;
-      const int64_t rb = sh ? rb_sd : rb_d;
+      const int rb = sh ? rb_sd : rb_d;
       const uint32_t bytes = uint32_t(DN_ROWS * rb);
       mbar_arrive_expect_tx(&full[s], bytes + hbytes);
       if (sh) bulk_load(dst, w.sdown + c0 * rb, bytes, &full[s]);
@@ -261,7 +276,8 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
         CK_TRACE(l, 13);
       }
       bulk_load(dst + S.hoff, static_cast<const uint8_t*>(A.h) + size_t(u) * hbytes, hbytes, &full[s]);
-      ++issued[s];
+      issued = it + 1;
+      CK_ITRACE(l, it - it_layer, 0);
     }
     if (!ok) break;
     CK_TRACE(l, 14);
@@ -269,8 +285,8 @@ __device__ void producer(const Args& A, uint8_t* smem, const Smem& S, int r_lo, 
     mbar_arrive(prod_done);
   }
   // leave no copy in flight: wait (bounded) for the last phase each stage was filled for
-  for (int s = 0; s < STAGES; ++s)
-    if (issued[s]) mbar_wait(&full[s], (issued[s] - 1) & 1, A.err);
+  for (uint32_t i = issued > uint32_t(STAGES) ? issued - STAGES : 0; i < issued; ++i)
+    mbar_wait(&full[i % STAGES], (i / STAGES) & 1, A.err);
 }
 
 // ---- consumers: a gate/up item is split over a group's eight warps by runs, four at a time (the three-kernel
@@ -295,10 +311,11 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const int T_ = A.T, H = A.H, E = A.E, K = A.K;
-  const Smem S = smem_of(T_, H, A.rt_rows, A.wmax, A.hstride);
+  const Smem S = smem_of(T_, H, A.rt_rows, A.wmax, A.hstride, A.stages);
+  const int STAGES = A.stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S.bars);
-  uint64_t* empty = full + STAGES;
-  uint64_t* rt_full = empty + STAGES;
+  uint64_t* empty = full + MAX_STAGES;
+  uint64_t* rt_full = empty + MAX_STAGES;
   uint64_t* rt_free = rt_full + 1;
   uint64_t* plan_ready = rt_free + 1;
   uint64_t* hready = plan_ready + 1;
@@ -347,8 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
 
   for (int l = 0; l < A.L; ++l) {
     const LayerW& w = A.w[l];
-    const int64_t rb_gu = row_bytes(w.kgu, H), rb_d = row_bytes(w.kd, A.I);
-    const int64_t rb_sd = A.Is ? row_bytes(w.kd, A.Is) : 0;
+    const int rb_gu = w.rb_gu, rb_d = w.rb_d, rb_sd = w.rb_sd;
     // ---- the window: the chain's input, or the previous layer's combined outputs
     if (tid == 0) CK_TRACE(l, 0);
     const bool fresh = l == 0 || (A.refeed > 0 && l % A.refeed == 0);
@@ -415,6 +431,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       CK_TRACE(l, 4);
     }
     const Items I_ = items_of(units, A.I, A.Is, H, cta, G);
+    const uint32_t it_layer = it;
     // ---- G: gate/up items; item `it` goes to the group of its stage's parity
     for (int j = I_.g0; j < I_.g1; ++j, ++it) {
       const int s = int(it % STAGES);
@@ -422,20 +439,20 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       int u, r0;
       I_.unit_row_gu(j, u, r0);
       const dl::Unit un = plan->unit[u];
-      const bool sh = u == 0 && A.Is > 0;
-      const int64_t rb = sh ? row_bytes(w.kgu, H) : rb_gu;
+      const int rb = rb_gu;  // the shared expert's gate / up rows are of the routed experts' kind
       const uint8_t* wg = stage0 + s * S.stage;
       const uint8_t* wu = wg + align16(int(RG * rb));
       float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
-      const bool got = mbar_wait(&full[s], (it / STAGES) & 1, A.err);
+      const bool got = mbar_wait_sleep(&full[s], (it / STAGES) & 1, A.err, WAIT_LIMIT, 20000);
+      if (gw == 0 && lane == 0) CK_ITRACE(l, it - it_layer, 1);
       if (got) {
         int n0, n1;
         gu_runs(H, gw, n0, n1);
         const int g = lane >> 2;
         const T* xg = g < T_ ? xs + g * (H + 32) : nullptr;
         by_kind(w.kgu, [&]<int KIND>() {
-          frag_runs<KIND, T>(wg + g * rb, wg + (g + 8) * rb, xg, n0, n1, lane, grid_tab<KIND>(tabs), accg);
-          frag_runs<KIND, T>(wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane, grid_tab<KIND>(tabs), accu);
+          frag_runs2<KIND, T>(wg + g * rb, wg + (g + 8) * rb, wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane,
+                              grid_tab<KIND>(tabs), accg, accu);
         });
       }
       __syncwarp();
@@ -467,6 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       }
       if (!got) s_abort = 1;
       named_sync(2 + grp, GW * 32);
+      if (gw == 0 && lane == 0) CK_ITRACE(l, it - it_layer, 2);
     }
     if (tid == 0) CK_TRACE(l, 5);
     if (!barrier()) return;  // B: every unit's h
@@ -482,11 +500,12 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
       I_.unit_row_dn(j, A.Is > 0, u, c0);
       const dl::Unit un = plan->unit[u];
       const bool sh = u == 0;
-      const int64_t rb = sh ? rb_sd : rb_d;
+      const int rb = sh ? rb_sd : rb_d;
       const uint8_t* st = stage0 + s * S.stage;
       const T* hs = reinterpret_cast<const T*>(st + S.hoff);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const bool got = mbar_wait(&full[s], (it / STAGES) & 1, A.err);
+      const bool got = mbar_wait_sleep(&full[s], (it / STAGES) & 1, A.err, WAIT_LIMIT, 20000);
+      if (gw == 0 && lane == 0) CK_ITRACE(l, it - it_layer, 1);
       if (got) {
         const int g = lane >> 2;
         const bool mine = g < T_ && ((un.tokmask >> g) & 1u);
@@ -511,6 +530,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
           Y[(int64_t(tok) * (K + 1) + k) * H + c0 + gw * 16 + m] = from_f32<T>(acc[q]);
         }
       }
+      if (gw == 0 && lane == 0) CK_ITRACE(l, it - it_layer, 2);
     }
     const bool last = l == A.L - 1;
     const bool next_fresh = !last && A.refeed > 0 && (l + 1) % A.refeed == 0;
@@ -524,13 +544,14 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
     T* dst = static_cast<T*>(last ? A.out : A.Xn);
     for (int q = q0 + tid; q < q1; q += CT) {
       const int tok = q / H, c = q % H;
-      float yk[TOPK_MAX_K + 1];
+      float yk[TOPK_MAX_K];
       const T* yt = Y + int64_t(tok) * (K + 1) * H + c;
 #pragma unroll
-      for (int k = 0; k <= TOPK_MAX_K; ++k)
-        if (k <= K) yk[k] = to_f32(__ldcg(yt + int64_t(k) * H));
+      for (int k = 0; k < TOPK_MAX_K; ++k)
+        if (k < K) yk[k] = to_f32(__ldcg(yt + int64_t(k) * H));
+      const float sv = A.Is > 0 ? to_f32(__ldcg(yt + int64_t(K) * H)) : 0.f;
       const float gv = A.Is > 0 ? round_to<T>(s_gsh[tok]) : -INFINITY;
-      dst[q] = from_f32<T>(combine_one<T>(yk, s_wts + tok * K, K, gv, A.Is > 0 ? yk[K] : 0.f));
+      dst[q] = from_f32<T>(combine_one<T>(yk, s_wts + tok * K, K, gv, sv));
     }
     if (tid == 0) CK_TRACE(l, 9);
     if (last) break;
@@ -611,6 +632,9 @@ using namespace sc;
 extern "C" SC_API int sc_chain_trace_read(void* host) {
   return cudaMemcpyFromSymbol(host, ck::g_ctrace, sizeof(ck::g_ctrace)) == cudaSuccess ? 0 : -1;
 }
+extern "C" SC_API int sc_chain_itrace_read(void* host) {
+  return cudaMemcpyFromSymbol(host, ck::g_itrace, sizeof(ck::g_itrace)) == cudaSuccess ? 0 : -1;
+}
 #endif
 
 extern "C" size_t sc_moe_decode_chain_workspace(const sc_moe_layer* layers, int n_layers, int tokens) {
@@ -663,6 +687,9 @@ extern "C" int sc_moe_decode_chain(const sc_moe_layer* layers, int n_layers, con
     w.shared_gate = static_cast<const __half*>(b.shared_gate);
     w.kgu = b.kind_gate;
     w.kd = b.kind_down;
+    w.rb_gu = int(row_bytes(b.kind_gate, b.hidden));
+    w.rb_d = int(row_bytes(b.kind_down, b.inter));
+    w.rb_sd = b.shared_inter ? int(row_bytes(b.kind_sdown, b.shared_inter)) : 0;
     const int gu = 2 * align16(int(ck::RG * row_bytes(b.kind_gate, b.hidden)));
     const int dn = int(ck::DN_ROWS * row_bytes(b.kind_down, b.inter));
     const int dns = b.shared_inter ? int(ck::DN_ROWS * row_bytes(b.kind_sdown, b.shared_inter)) : 0;
@@ -680,7 +707,11 @@ extern "C" int sc_moe_decode_chain(const sc_moe_layer* layers, int n_layers, con
   A.h = ws + m.h;
   A.Y = ws + m.Y;
   A.Xn = ws + m.Xn;
-  const ck::Smem S = ck::smem_of(tokens, a.hidden, A.rt_rows, wmax, A.hstride);
+  // as many stages as fit (an even number, 4 .. 8): small windows then fetch every item of a layer at once
+  const ck::Smem S0 = ck::smem_of(tokens, a.hidden, A.rt_rows, wmax, A.hstride, 0);
+  A.stages = std::min(ck::MAX_STAGES, ((227 * 1024 - 256 - S0.total) / S0.stage) & ~1);
+  if (A.stages < 4) return SC_ERR_SHAPE;
+  const ck::Smem S = ck::smem_of(tokens, a.hidden, A.rt_rows, wmax, A.hstride, A.stages);
   // one block an SM: more than half an SM's shared memory keeps a second block off
   const int smem = std::max(S.total, 116 * 1024);
   if (smem > 227 * 1024) return SC_ERR_SHAPE;

@@ -251,8 +251,8 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
   if (!mbar_wait(bar, 0, L.err)) return;
   TRACE_POINT(1, 3);
-  frag_runs<KIND, T>(wg + g * rb, wg + (g + 8) * rb, xg, n0, n1, lane, tab, accg);
-  frag_runs<KIND, T>(wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane, tab, accu);
+  frag_runs2<KIND, T>(wg + g * rb, wg + (g + 8) * rb, wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane, tab, accg,
+                      accu);
   TRACE_POINT(1, 4);
   // red[value][warp][lane]: the reducing thread (value q, lane L) reads eight consecutive words
   red[((0 + 0) * WARPS + warp) * 32 + lane] = accg[0];

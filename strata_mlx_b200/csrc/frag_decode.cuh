@@ -6,10 +6,10 @@
 // to the run's float32 sums afterwards, so that products and sums are those of a float32 accumulation of the
 // reference's weights (strata_mlx/blocks.py:57-115), to the tensor core's rounding:
 //   Q2_0     (blocks.py:58-67) w = d (c - 1): the 2-bit code c is masked into the mantissa next to a power-of-two
-//            bias B (one LOP3 a register of two weights, no subtraction); the biases' sum is taken off by a second
-//            product of the same activations with the constant -(B + 1) (the + 1 is the code's - 1), so that the
-//            run's sum is sum (c - 1) x. A lane's register q holds weights q and q + 4 of its eight (the codes of
-//            both sit at bits 2q of the two code bytes); activations are staged in that order (x_pairs).
+//            bias B (one LOP3 a register of two weights, the code at bits 2q where B's mantissa unit is 1), and
+//            B + 1 taken off in one exact 16-bit add: c - 1. A lane's register q holds weights q and q + 4 of its
+//            eight (both codes sit at bits 2q of the two code bytes); activations are staged in that order
+//            (x_pairs). A block's d scales the float32 sums of its two runs at once.
 //   IQ3_S    (blocks.py:89-101) and IQ3_XXS (:103-115): the grid entry's four values are read as four 16-bit
 //            floats from an expanded codebook in shared memory (one 8-byte load an entry), the signs XORed into
 //            bits 15 and 31 (an IMAD and a LOP3 a register); registers hold weights (0,1) (2,3) (4,5) (6,7) of the
@@ -88,6 +88,16 @@ template <> struct Q2<__half> {  // B = 1024, 256, 64, 16: every pair fits the 1
   static constexpr bool shift3 = false;
 };
 
+template <typename T> __device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b);
+template <> __device__ __forceinline__ uint32_t add2<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hadd2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+template <> __device__ __forceinline__ uint32_t add2<__half>(uint32_t a, uint32_t b) {
+  __half2 r = __hadd2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
 // sign bits j and j + 1 of a lane's sign byte into bits 15 and 31 of its register r (j = 2r)
 __device__ __forceinline__ uint32_t signs_of(uint32_t s8, int r) {
   const uint32_t m = r == 0 ? 0x40008000u : r == 1 ? 0x10002000u : r == 2 ? 0x04000800u : 0x01000200u;
@@ -122,17 +132,13 @@ __device__ __forceinline__ void frag_runs(const uint8_t* ra, const uint8_t* rb, 
           const uint32_t ub = __byte_perm(ld_u16(bb + 2 + 8 * h + 2 * t), 0, 0x4140);
           uint32_t pa[4], pb[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 4; ++q) {  // B + c, less B + 1 in one exact subtraction: c - 1
             const uint32_t sa = (Q2<T>::shift3 && q == 3) ? ua >> 4 : ua;
             const uint32_t sb = (Q2<T>::shift3 && q == 3) ? ub >> 4 : ub;
-            pa[q] = (sa & Q2<T>::mask(q)) | Q2<T>::expo(q);
-            pb[q] = (sb & Q2<T>::mask(q)) | Q2<T>::expo(q);
+            pa[q] = add2<T>((sa & Q2<T>::mask(q)) | Q2<T>::expo(q), Q2<T>::neg(q));
+            pb[q] = add2<T>((sb & Q2<T>::mask(q)) | Q2<T>::expo(q), Q2<T>::neg(q));
           }
-          const uint32_t n0f[4] = {Q2<T>::neg(0), Q2<T>::neg(0), Q2<T>::neg(1), Q2<T>::neg(1)};
-          const uint32_t n1f[4] = {Q2<T>::neg(2), Q2<T>::neg(2), Q2<T>::neg(3), Q2<T>::neg(3)};
           const uint32_t a0[4] = {pa[0], pb[0], pa[1], pb[1]}, a1[4] = {pa[2], pb[2], pa[3], pb[3]};
-          mma16816<T>(d, n0f, xr.x, xr.y);
-          mma16816<T>(d, n1f, xr.z, xr.w);
           mma16816<T>(d, a0, xr.x, xr.y);
           mma16816<T>(d, a1, xr.z, xr.w);
         }
@@ -195,6 +201,18 @@ __device__ __forceinline__ void frag_runs(const uint8_t* ra, const uint8_t* rb, 
         acc[2] = fmaf(sb, d[2], acc[2]); acc[3] = fmaf(sb, d[3], acc[3]);
       }
     }
+  }
+}
+
+// Two products against the same activations at once (a gate/up item's gate rows and up rows), each run's decodes of
+// both interleaved: the same sums, in the same order, as two frag_runs calls.
+template <int KIND, typename T>
+__device__ __forceinline__ void frag_runs2(const uint8_t* ga, const uint8_t* gb, const uint8_t* ua, const uint8_t* ub,
+                                           const T* xg, int n0, int n1, int lane, const uint2* tab,
+                                           float (&accg)[4], float (&accu)[4]) {
+  for (int n = n0; n < n1; n += 4) {
+    frag_runs<KIND, T>(ga, gb, xg, n, n + 4, lane, tab, accg);
+    frag_runs<KIND, T>(ua, ub, xg, n, n + 4, lane, tab, accu);
   }
 }
 
