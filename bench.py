@@ -366,14 +366,23 @@ def run_ep(args, world, rank, local) -> None:
             "gpu_launches": (4 * args.layers + (1 if chain is not None else 0)) * args.steps,
             "gpu_launches_per_step": 4 * args.layers + (1 if chain is not None else 0), "clocks": clk}
     line["graph"] = graph is not None
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     del graph
     torch.cuda.synchronize()
     barrier(world)
     if chain is not None:
         chain.check_errors()
         chain.close()
+    del layers, chain
+    torch.cuda.empty_cache()
+    if not args.no_extra:
+        line["config4"] = config4_result(world, rank, device, group=dist.group.WORLD)
+        barrier(world)
+        line["config5"] = config5_result(world, rank, device, group=dist.group.WORLD, steps=args.config5_steps)
+        barrier(world)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    barrier(world)
     dist.destroy_process_group()
 
 
@@ -600,6 +609,152 @@ def prefill_cpu_sample(pairs: int, flops: float, seconds: float = 10.0) -> dict:
     per_pair = (time.perf_counter() - t0) / n
     return {"value": flops / (per_pair * pairs) / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"{n} pairs' gate, up and down products timed (~{seconds:.0f} s), scaled to {pairs} pairs"}
+
+
+# ---- configurations 4 and 5: the synthetic decoder around the MoE blocks
+
+
+def decoder_bytes(dec, routes_per_layer: list, ctx: int, world: int) -> float:
+    """Bytes a rank reads in one pass: its share of the window's distinct experts (routes counted per layer), the
+    shared expert, the router, the dense projections and the key/value cache up to `ctx` (all replicated)."""
+    total = dec.dense_bytes + 2 * dec.vocab * dec.hidden  # projections; output head (bf16) and embedding rows
+    for (per_expert, shared), used in zip(dec.expert_bytes, routes_per_layer):
+        total += used * per_expert / world + shared + E * H * 2
+    total += dec.n_layers * ctx * dec.kv_heads * 256 * 2 * 2
+    return float(total)
+
+
+def graph_of(fn, device):
+    """fn captured as a CUDA graph on a side stream (after one warm call); returns (graph, its output)."""
+    st = torch.cuda.Stream(device=device)
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        out = fn()
+    torch.cuda.synchronize()
+    return g, out
+
+
+def config4_result(world: int, rank: int, device, group=None, passes: int = 20) -> dict:
+    """Configuration 4: a verify pass of 1 + 4 tokens through 48 layers (attention 16 q / 2 kv heads of 256 over an
+    8K context in 16-token pages, then the configuration-2 MoE block, experts Q2_0 / IQ3_S by layer), the experts
+    sharded over the ranks (every rank holds the window; an NCCL all-reduce of the pairs' outputs a layer). The cache
+    is filled with random keys and values (standing in for the prefill of an 8K prompt of random tokens). tok/s =
+    5 / pass time; the pass replays from a CUDA graph at the same position."""
+    from strata_mlx_b200 import decoder as D
+
+    T, CTX = 5, 8192
+    dec = D.SyntheticDecoder(48, ["Q2_0", "IQ3_S"], dense="bf16", device=device, group=group, mode="replicated",
+                             max_pos=CTX + 64)
+    cache = dec.cache(CTX + 16)
+    cache.fill_random(CTX - T)
+    g = torch.Generator(device=device)
+    g.manual_seed(44)
+    toks = torch.randint(0, dec.vocab, (T,), generator=g, device=device)
+    graph, logits = graph_of(lambda: dec.forward(toks, cache), device)
+    s = torch.cuda.current_stream()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = Clocks(device.index)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(passes):
+        graph.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = reduce_max(e0.elapsed_time(e1) / passes, world)
+    dec.check_errors()
+    used = [int(torch.unique(L["base"].routes(T, device)[0].view(torch.int32)).numel()) for L in dec.layers]
+    nbytes = decoder_bytes(dec, used, CTX, world)
+    pk = peaks()
+    top1 = logits.argmax(-1).tolist()
+    res = {"workload": "config4: speculative verify pass of 1 + 4 tokens, 48-layer synthetic MoE decoder (per layer "
+                       "GQA attention 16 q / 2 kv heads of 256 with RoPE over a paged 8K cache, 16-token pages, bf16 "
+                       "projections; the config-2 MoE block, experts Q2_0 / IQ3_S by layer)",
+           "tok_per_s": T / (ms * 1e-3), "ms_per_pass": ms, "tokens_per_pass": T, "context": CTX,
+           "parallelism": f"ep{world}: experts sharded, attention and dense replicated, NCCL all-reduce of the "
+                          "pairs' outputs per layer" if world > 1 else "single",
+           "roofline": {"bound": "hbm", "bytes_per_pass_per_rank": nbytes, "achieved": nbytes / (ms * 1e-3) / 1e9,
+                        "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                        "what": "a rank's share of the window's distinct experts + shared expert + router + dense "
+                                "projections + KV cache read, per pass"},
+           "distinct_experts_per_layer_mean": float(np.mean(used)), "top1": top1,
+           "kv_prefill": "random keys and values stand in for the prefill of the random-token prompt",
+           "graph": True, "clocks": clk}
+    del graph, dec, cache
+    torch.cuda.empty_cache()
+    return res
+
+
+def config5_result(world: int, rank: int, device, group=None, steps: int = 256, ctx: int = 131072) -> dict:
+    """Configuration 5: greedy decode of `steps` tokens for a batch of `world` sequences (one a rank) at a 128K
+    context, 48 layers cycling Q2_0 / IQ3_S / IQ3_XXS experts, Q8_0 dense projections (through the library's window
+    matvec). The MoE block's window is every rank's token (expert parallel: all-gather, all-reduce). Each step --
+    every layer, the head, the argmax, the next token and the position -- replays from a CUDA graph. The caches are
+    filled with random keys and values (standing in for the prefill of 128K-token random prompts)."""
+    from strata_mlx_b200 import decoder as D
+
+    dec = D.SyntheticDecoder(48, ["Q2_0", "IQ3_S", "IQ3_XXS"], dense="Q8_0", device=device, group=group,
+                             mode="per_rank", max_pos=ctx + steps + 64, seed=5)
+    cache = dec.cache(ctx + steps + 16, seed=rank)
+    cache.fill_random(ctx, seed=100 + rank)
+    g = torch.Generator(device=device)
+    g.manual_seed(55 + rank)
+    tok = torch.randint(0, dec.vocab, (1,), generator=g, device=device)
+    out = torch.zeros(steps, dtype=torch.int64, device=device)
+    step_i = torch.zeros(1, dtype=torch.int64, device=device)
+
+    def step():
+        logits = dec.forward(tok, cache)
+        nxt = logits.argmax(-1)
+        out.index_copy_(0, step_i, nxt)
+        tok.copy_(nxt)
+        cache.pos.add_(1)
+        step_i.add_(1)
+        return nxt
+
+    graph, _ = graph_of(step, device)
+    # the warm call and the capture moved nothing on the device that the replays depend on except pos and step_i
+    cache.pos.fill_(ctx)
+    step_i.zero_()
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.current_stream()
+    clocks = Clocks(device.index)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = reduce_max(e0.elapsed_time(e1) / steps, world)
+    dec.check_errors()
+    pk = peaks()
+    used = [world * 10] * dec.n_layers  # at most 10 distinct experts a token
+    nbytes = decoder_bytes(dec, used, ctx + steps // 2, world)
+    res = {"workload": "config5: greedy decode of 256 tokens at a 128K context, batch = one sequence a rank, 48-layer "
+                       "synthetic MoE decoder (GQA 16 q / 2 kv heads of 256, paged cache of 16-token pages, Q8_0 "
+                       "projections), experts cycling Q2_0 / IQ3_S / IQ3_XXS by layer",
+           "tok_per_s": world / (ms * 1e-3), "ms_per_step": ms, "steps": steps, "context": ctx, "batch": world,
+           "parallelism": f"ep{world}: experts sharded, the MoE window is every rank's token (NCCL all-gather + "
+                          "all-reduce), attention per rank" if world > 1 else "single",
+           "roofline": {"bound": "hbm", "bytes_per_step_per_rank": nbytes, "achieved": nbytes / (ms * 1e-3) / 1e9,
+                        "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                        "what": "KV cache read (12.9 GB a step) + Q8_0 projections + the rank's share of at most "
+                                "10 experts a token + shared expert + router, per step"},
+           "first_tokens": out[:8].tolist(),
+           "kv_prefill": "random keys and values stand in for the prefill of 128K-token random prompts",
+           "graph": True, "clocks": clk}
+    del graph, dec, cache
+    torch.cuda.empty_cache()
+    return res
 
 
 def stage_bytes(kind: str) -> dict:
@@ -844,6 +999,7 @@ def main() -> None:
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
                     help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config5-steps", type=int, default=256, help="greedy decode steps of the configuration-5 line")
     ap.add_argument("--no-extra", action="store_true",
                     help="leave out the configuration-1 and configuration-3 sub-lines of the one-GPU decode line")
     ap.add_argument("--no-graph", action="store_true",
@@ -957,6 +1113,8 @@ def main() -> None:
         torch.cuda.synchronize()
         line["config1"] = config1_result(cpu_seconds=None if args.no_cpu_baseline else 5.0)
         line["prefill"] = prefill_result(20, 5, None if args.no_cpu_baseline else 6.0)
+        line["config4"] = config4_result(world, rank, device)
+        line["config5"] = config5_result(world, rank, device, steps=args.config5_steps)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cb = cpu_sample(args.kinds, 12.0, True)
         cpu_ms = step_seconds(cb["per_layer_s"], args.layers, args.kinds) * 1000.0

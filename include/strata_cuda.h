@@ -268,6 +268,20 @@ SC_API int sc_moe_decode_layer_ep_p2p(const sc_moe_layer* layer, const sc_ep_exc
 SC_API int sc_ep_combine(const sc_moe_layer* layer, const sc_ep_exchange* ex, int parity, int last, void* out,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Paged grouped-query attention of the synthetic decoder around the MoE blocks (strata_mlx's engine runs its own
+ * attention trunk, strata_mlx/engine.py:710-749; the decoder here stands in for it at BASELINE configurations 4 and
+ * 5, whose MoE blocks are the hot path). One sequence: q (tokens, q_heads, head_dim) bfloat16 of the window's
+ * `tokens` (1..8) new tokens; the cache k_cache, v_cache (pages, 16, kv_heads, head_dim) bfloat16, the sequence's
+ * pages listed in block_table; *ctx_dev (device int, at most max_ctx, read by the kernels so that a decode step can
+ * replay from a CUDA graph) tokens in all, the window's own keys already written at positions ctx - tokens ..
+ * ctx - 1. Token i sees keys 0 .. ctx - tokens + i. out (tokens, q_heads, head_dim) bfloat16 = softmax(scale q k^T) v,
+ * float32 sums, probabilities rounded to bfloat16 for the value product. head_dim 256, q_heads = 8 kv_heads.
+ * workspace: sc_paged_attention_workspace(max_ctx, kv_heads) bytes. */
+SC_API int sc_paged_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                              const int32_t* ctx_dev, int max_ctx, int tokens, int q_heads, int kv_heads, int head_dim,
+                              float scale, void* out, void* workspace, size_t workspace_bytes, void* stream);
+SC_API size_t sc_paged_attention_workspace(int ctx, int kv_heads);
+
 /* No counterpart in strata-mlx: an addition for callers that cannot allocate device memory.
  *
  * sc_moe_decode_layer without a workspace argument. Some hosts of this library own every byte of device memory
