@@ -268,7 +268,7 @@ class SyntheticDecoder:
             self._ws = torch.empty(n, dtype=torch.uint8, device=self.device)
         return self._ws
 
-    def forward(self, tokens: torch.Tensor, cache: PagedCache) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, cache: PagedCache, trace: list | None = None) -> torch.Tensor:
         """The window `tokens` (t,) int64 on the device at the cache's position: every layer (their keys and values
         written at positions pos .. pos + t - 1), then the output head. Returns logits (t, vocab) float32. Does not
         move the position (advance does), so that a verify pass can be replayed at the same place."""
@@ -278,9 +278,13 @@ class SyntheticDecoder:
         slots = cache.slots(t)
         x = self.embed.index_select(0, tokens)
         for l, L in enumerate(self.layers):
+            if trace is not None:
+                trace.append(x.clone())  # each layer's input, for tests that check a layer at a time
             h = rmsnorm(x, L["n1"])
             x = x + L["attn"](h, cache, l, self.rope, ws, positions, slots)
             x = x + L["moe"](rmsnorm(x, L["n2"]))
+        if trace is not None:
+            trace.append(x.clone())
         return rmsnorm(x, self.final_norm).float() @ self.head_f32.T
 
     @staticmethod
@@ -293,54 +297,61 @@ class SyntheticDecoder:
         _lib.check_device_errors()
 
 
-def oracle_forward(dec: SyntheticDecoder, tokens: np.ndarray, cache_k: list, cache_v: list, pos: int,
-                   blocks: list) -> np.ndarray:
-    """The decoder's pass in float32 numpy/torch on the CPU with the GPU's bfloat16 rounding points: dense products
-    in float32 rounded to bfloat16, attention in float32 (softmax of the scaled scores, probabilities rounded to
-    bfloat16 as the kernel does), the MoE block by the oracle (oracle/blocks_ref.py moe_layer_blocks). TEST
-    INFRASTRUCTURE: used by tests only. cache_k/v[l]: (pos, kv_heads, D) float32 of the positions before the window;
-    blocks[l]: the layer's blocks as synthetic.layer_numpy's dict (all experts)."""
+def _bf(a):
     from oracle import blocks_ref as R
 
-    def bf(a):
-        return R.round_to(np.asarray(a, dtype=np.float32), "bfloat16")
+    return R.round_to(np.asarray(a, dtype=np.float32), "bfloat16")
 
-    def norm(a):
-        a = np.asarray(a, dtype=np.float32)
-        return bf(a / np.sqrt((a * a).mean(-1, keepdims=True) + np.float32(1e-6)))
 
-    t = len(tokens)
-    H = dec.hidden
-    x = dec.embed.float().cpu().numpy()[tokens]
+def _norm(a):
+    a = np.asarray(a, dtype=np.float32)
+    return _bf(a / np.sqrt((a * a).mean(-1, keepdims=True) + np.float32(1e-6)))
+
+
+def oracle_layer(dec: SyntheticDecoder, l: int, x: np.ndarray, pos: int, cache_k: list, cache_v: list,
+                 blocks: dict) -> tuple:
+    """Layer l of the decoder in float32 numpy on the CPU with the GPU's bfloat16 rounding points, for the window x
+    (t, hidden) (values of bfloat16) at positions pos .. pos + t - 1: dense products in float64 rounded to bfloat16,
+    attention in float64 (the probabilities rounded to bfloat16 as the kernel rounds them), the MoE block by the
+    oracle (oracle/blocks_ref.py moe_layer_blocks, on every expert of `blocks`, synthetic.layer_numpy's form). The
+    layer's keys and values are appended to cache_k[l] / cache_v[l] ((positions, kv_heads, D) float32). Returns
+    (output, the MoE block's parts). TEST INFRASTRUCTURE: used by tests only."""
+    from oracle import blocks_ref as R
+
+    t = x.shape[0]
+    A = dec.layers[l]["attn"]
     cos, sin = dec.rope.cos.cpu().numpy(), dec.rope.sin.cpu().numpy()
     positions = np.arange(pos, pos + t)
 
     def rope(a):
         c, s = cos[positions][:, None, :], sin[positions][:, None, :]
         h1, h2 = a[..., : HEAD_DIM // 2], a[..., HEAD_DIM // 2 :]
-        return bf(np.concatenate([h1 * c - h2 * s, h2 * c + h1 * s], axis=-1))
+        return _bf(np.concatenate([h1 * c - h2 * s, h2 * c + h1 * s], axis=-1))
 
-    for l, L in enumerate(dec.layers):
-        A = L["attn"]
-        h = norm(x)
-        mm = lambda d, a: bf(a.astype(np.float64) @ d.floats().cpu().numpy().astype(np.float64).T)
-        q = rope(mm(A.wq, h).reshape(t, A.hq, HEAD_DIM))
-        k = rope(mm(A.wk, h).reshape(t, A.hkv, HEAD_DIM))
-        v = mm(A.wv, h).reshape(t, A.hkv, HEAD_DIM)
-        K = np.concatenate([cache_k[l], k], 0)  # (pos + t, hkv, D)
-        V = np.concatenate([cache_v[l], v], 0)
-        o = np.zeros((t, A.hq, HEAD_DIM), dtype=np.float32)
-        for i in range(t):
-            n = pos + i + 1
-            for hh in range(A.hq):
-                kv = hh // (A.hq // A.hkv)
-                s = (K[:n, kv].astype(np.float64) @ q[i, hh].astype(np.float64)) / math.sqrt(HEAD_DIM)
-                p = np.exp(s - s.max())
-                o[i, hh] = (bf(p) @ V[:n, kv].astype(np.float64)) / p.sum()
-        o = bf(o)
-        x = bf(x + mm(A.wo, o.reshape(t, -1)))
-        parts = R.moe_layer_blocks(norm(x), blocks[l], H, blocks[l]["inter"], blocks[l]["top_k"], "bfloat16",
-                                   shared_inter=blocks[l]["shared_inter"])
-        x = bf(x + parts["out"])
-        cache_k[l], cache_v[l] = K, V
-    return norm(x).astype(np.float64) @ dec.head.float().cpu().numpy().astype(np.float64).T
+    def mm(d, a):
+        return _bf(a.astype(np.float64) @ d.floats().cpu().numpy().astype(np.float64).T)
+
+    h = _norm(x)
+    q = rope(mm(A.wq, h).reshape(t, A.hq, HEAD_DIM))
+    k = rope(mm(A.wk, h).reshape(t, A.hkv, HEAD_DIM))
+    v = mm(A.wv, h).reshape(t, A.hkv, HEAD_DIM)
+    K = np.concatenate([cache_k[l], k], 0)
+    V = np.concatenate([cache_v[l], v], 0)
+    o = np.zeros((t, A.hq, HEAD_DIM), dtype=np.float32)
+    for i in range(t):
+        n = pos + i + 1
+        for hh in range(A.hq):
+            kv = hh // (A.hq // A.hkv)
+            sc = (K[:n, kv].astype(np.float64) @ q[i, hh].astype(np.float64)) / math.sqrt(HEAD_DIM)
+            p = np.exp(sc - sc.max())
+            o[i, hh] = (_bf(p) @ V[:n, kv].astype(np.float64)) / p.sum()
+    x = _bf(x + mm(A.wo, _bf(o).reshape(t, -1)))
+    parts = R.moe_layer_blocks(_norm(x), blocks, dec.hidden, blocks["inter"], blocks["top_k"], "bfloat16",
+                               shared_inter=blocks["shared_inter"])
+    cache_k[l], cache_v[l] = K, V
+    return _bf(x + parts["out"]), parts
+
+
+def oracle_head(dec: SyntheticDecoder, x: np.ndarray) -> np.ndarray:
+    """The output head on the last layer's output: float64 logits of the normed window. TEST INFRASTRUCTURE."""
+    return _norm(x).astype(np.float64) @ dec.head.float().cpu().numpy().astype(np.float64).T
