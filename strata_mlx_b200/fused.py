@@ -20,6 +20,12 @@ ROUTER_AS_IS = True  # fused.py:421
 COMBINE_UPTO = 16  # fused.py:464: tokens the combine kernel takes; more go through torch's operations
 
 
+def _device(device) -> torch.device:
+    """A CUDA device with its index ("cuda" names the current one), so that workspaces are keyed alike."""
+    d = torch.device(device)
+    return torch.device(d.type, torch.cuda.current_device()) if d.type == "cuda" and d.index is None else d
+
+
 class WindowLinear:
     """A float16 linear layer without bias whose products come back in float32; a window of up to `upto` tokens
     goes through the router kernel, which reads the weights once as they are (fused.py:357-390)."""
@@ -177,6 +183,7 @@ class MoEDecodeLayer:
         self._ws: dict = {}
 
     def workspace(self, tokens: int, device) -> torch.Tensor:
+        device = _device(device)
         ws = self._ws.get((tokens, device))
         if ws is None:
             n = _lib.lib().sc_moe_decode_workspace(self.layer_ref(), tokens)
@@ -261,6 +268,7 @@ class DecodeChain:
         return ctypes.addressof(self._structs)
 
     def workspace(self, tokens: int, device) -> torch.Tensor:
+        device = _device(device)
         ws = self._ws.get((tokens, device))
         if ws is None:
             n = _lib.lib().sc_moe_decode_chain_workspace(self._ref(), len(self.layers), tokens)
