@@ -124,8 +124,18 @@ class BlockSwitchLinear:
         return out.reshape(*indices.shape, 1, self.output_dims)
 
     def _as_floats(self, x: torch.Tensor, indices: torch.Tensor, share: int) -> torch.Tensor:
-        """The stack dequantized to the activations' type, then a product per expert (the reference's
-        gather_mm, blocks.py:438-440)."""
+        """Many pairs at once (the reference unpacks the stack for MLX's gather_mm, blocks.py:438-440). For a stack
+        the tile products take, the pairs go through tiles_of and tile_matmul on the GPU, weights rounded to the
+        activations' type as gather_mm's are: no host synchronization. Other shapes: the stack dequantized and a
+        product per expert."""
+        if x.dtype in (torch.float16, torch.bfloat16) and tileable(self.kind, self.output_dims, self.input_dims):
+            flat = indices.reshape(-1, 1)
+            tiles, token, where = tiles_of(flat, self.num_experts)
+            xs = x.reshape(-1, self.input_dims)
+            a = xs.index_select(0, token.to(torch.int64) // share)  # a slot's pair p reads input row p // share
+            c = tile_matmul(self.blocks, self.kind, (self.num_experts, self.output_dims, self.input_dims), a, tiles)
+            out = c.index_select(0, where.to(torch.int64)).to(x.dtype)
+            return out.reshape(*indices.shape, 1, self.output_dims)
         w = dequantize(self.blocks, self.kind, (self.num_experts, self.output_dims, self.input_dims), x.dtype)
         flat = indices.reshape(-1).long()
         xs = x.reshape(-1, self.input_dims)

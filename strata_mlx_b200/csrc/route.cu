@@ -25,6 +25,51 @@ __global__ void __launch_bounds__(256) router_kernel(const __half* __restrict__ 
   }
 }
 
+// ---- router for a chunk of a prompt (more than ROUTER_MAX_TOKENS tokens): logits (tokens, rows) = x . W^T as a
+// tiled product on the CUDA cores, 64 tokens x 64 rows a block, 4 x 4 a thread, float32 sums of the float16 weights
+// and the activations (the reference multiplies floats here, fused.py:386-388 through the layer's own product)
+
+constexpr int RTB = 64, RKB = 32;
+
+template <typename InT>
+__global__ void __launch_bounds__(256) router_tile_kernel(const __half* __restrict__ w, int rows, int cols,
+                                                          const InT* __restrict__ x, int tokens,
+                                                          float* __restrict__ out) {
+  __shared__ float xs[RKB][RTB + 4], ws[RKB][RTB + 4];
+  const int t0 = blockIdx.y * RTB, r0 = blockIdx.x * RTB;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // outputs: tokens t0 + 4 ty .., rows r0 + 4 tx ..
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < cols; k0 += RKB) {
+    for (int i = threadIdx.x; i < RTB * RKB; i += 256) {
+      const int a = i / RKB, k = i % RKB;
+      xs[k][a] = (t0 + a < tokens && k0 + k < cols) ? to_f32(x[int64_t(t0 + a) * cols + k0 + k]) : 0.f;
+      ws[k][a] = (r0 + a < rows && k0 + k < cols) ? __half2float(w[int64_t(r0 + a) * cols + k0 + k]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < RKB; ++k) {
+      float xa[4], wb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xa[j] = xs[k][4 * ty + j];
+        wb[j] = ws[k][4 * tx + j];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wb[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = t0 + 4 * ty + i, r = r0 + 4 * tx + j;
+      if (t < tokens && r < rows) out[int64_t(t) * rows + r] = acc[i][j];
+    }
+}
+
 // ---- top-k (+ softmax): one warp per row of logits
 
 __global__ void topk_kernel(const float* __restrict__ logits, int rows, int n, int k, uint32_t* __restrict__ idx,
@@ -82,6 +127,15 @@ extern "C" int sc_router(const void* w, int rows, int cols, const void* x, int d
   if (cols % 8 || (reinterpret_cast<uintptr_t>(w) & 15)) return SC_ERR_ALIGN;
   if (rows == 0 || tokens == 0) return SC_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (tokens > ROUTER_MAX_TOKENS) {  // a chunk of a prompt: the tiled product, the weights read once a 64 tokens
+    const dim3 grid(unsigned(ceil_div(rows, RTB)), unsigned(ceil_div(tokens, RTB)));
+    bool ok = dispatch_dtype(dtype, [&]<typename InT>() {
+      router_tile_kernel<InT><<<grid, 256, 0, s>>>(static_cast<const __half*>(w), rows, cols,
+                                                    static_cast<const InT*>(x), tokens, logits);
+    });
+    if (!ok) return SC_ERR_DTYPE;
+    return launch_rc();
+  }
   // windows of up to ROUTER_MAX_TOKENS tokens whose float32 activations fit shared memory
   const int per = std::max(1, std::min(ROUTER_MAX_TOKENS, int((96 * 1024) / (int64_t(cols) * 4))));
   const int grid = int(std::min<int64_t>(ceil_div(rows, 8), 148 * 4));

@@ -48,6 +48,17 @@ class WindowLinear:
         require_cuda(x)
         tokens = x.numel() // self.cols
         if not self.takes(x):
+            w = self.weight
+            if w.dtype == torch.float16 and self.cols % 8 == 0 and x.dtype in DTYPES:
+                # a chunk of a prompt: the reference multiplies floats here (fused.py:386-388); sc_router's tiled
+                # product takes the float16 weights as they are, float32 sums
+                xs = x.reshape(tokens, self.cols)
+                xs = xs if xs.is_contiguous() else xs.contiguous()
+                w = w if w.is_contiguous() else w.contiguous()
+                out = torch.empty((tokens, self.rows), dtype=torch.float32, device=x.device)
+                check(_lib.lib().sc_router(ptr(w), self.rows, self.cols, ptr(xs), DTYPES[xs.dtype], tokens, ptr(out),
+                                           stream()), "WindowLinear")
+                return out.reshape(*x.shape[:-1], self.rows)
             if isinstance(self.linear, torch.Tensor):
                 return x.float() @ self.linear.float().T
             return self.linear(x)
@@ -104,6 +115,19 @@ def moe_combine(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tens
     return out.reshape(*lead, d)
 
 
+def _combine_rows(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """sc_moe_combine over any number of rows (the combine of a prompt chunk's tokens), MLX's add order of
+    fused.py:448-462 kept for every row."""
+    *lead, k, d = y.shape
+    rows = y.numel() // (k * d)
+    out = torch.empty((rows, d), dtype=y.dtype, device=y.device)
+    yy, ww = y.reshape(rows, k, d).contiguous(), w.reshape(rows, k).float().contiguous()
+    gg, ss = g.reshape(rows).to(y.dtype).contiguous(), s.reshape(rows, d).to(y.dtype).contiguous()
+    check(_lib.lib().sc_moe_combine(ptr(yy), ptr(ww), ptr(gg), ptr(ss), rows, k, d, DTYPES[y.dtype], ptr(out), stream()),
+          "moe_combine")
+    return out.reshape(*lead, d)
+
+
 class SharedExpert:
     """The block's shared expert, an MLP on block weights (mlx-lm's MLP with gate_proj, up_proj, down_proj): each
     projection is a BlockSwitchLinear of one expert."""
@@ -112,10 +136,17 @@ class SharedExpert:
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        from .blocks import window_matvec
+        from .blocks import BlockSwitchLinear, TILES_FROM, switch_glu, tileable, window_matvec
 
         lead = x.shape[:-1]
         xs = x.reshape(-1, x.shape[-1])
+        lins = (self.gate_proj, self.up_proj, self.down_proj)
+        if (xs.shape[0] >= TILES_FROM and all(isinstance(l, BlockSwitchLinear) for l in lins)
+                and all(tileable(l.kind, l.output_dims, l.input_dims) for l in lins)):
+            # a chunk of a prompt: the expert as a stack of one through the tile products (the tcgen05 kernel)
+            idx = torch.zeros((xs.shape[0], 1), dtype=torch.int32, device=x.device)
+            out = switch_glu(xs, idx, self.up_proj, self.gate_proj, self.down_proj)
+            return out.reshape(*lead, -1)
         g = window_matvec(self.gate_proj.blocks, self.gate_proj.kind, self.gate_proj.output_dims, self.gate_proj.input_dims, xs)
         u = window_matvec(self.up_proj.blocks, self.up_proj.kind, self.up_proj.output_dims, self.up_proj.input_dims, xs)
         from .blocks import swiglu
@@ -153,6 +184,8 @@ class RoutedMoE:
             g = torch.full((*x.shape[:-1], 1), float("-inf"), dtype=x.dtype, device=x.device)
             s = torch.zeros_like(x)
         out = moe_combine(y, w, g, s) if COMBINE_UPTO else None
+        if out is None and COMBINE_UPTO and y.dtype in (torch.float16, torch.bfloat16) and y.shape[-2] <= 16:
+            out = _combine_rows(y, w, g, s)  # a chunk of a prompt: the same kernel and add order for every row
         if out is None:
             out = (y.float() * w[..., None]).sum(dim=-2).to(x.dtype) + torch.sigmoid(g) * s
         return out
