@@ -282,6 +282,19 @@ SC_API int sc_paged_attention(const void* q, const void* k_cache, const void* v_
                               float scale, void* out, void* workspace, size_t workspace_bytes, void* stream);
 SC_API size_t sc_paged_attention_workspace(int ctx, int kv_heads);
 
+/* The synthetic decoder's trunk (no counterpart in strata-mlx's MoE path; its engine's own trunk is out of scope):
+ * sc_add_rmsnorm: x (rows, cols) += delta (rounded to the type; delta may be NULL), then out = x * rsqrt(mean(x^2) +
+ * eps) * w, float32 math, cols by 8 (at most 8192), 16-byte aligned. sc_rope_cache: rotate-half RoPE on q (tokens,
+ * q_heads, head_dim) in place and on k (tokens, kv_heads, head_dim), the angles' cos / sin tables (positions,
+ * head_dim / 2) float32 at positions *pos .. *pos + tokens - 1 (pos a device int), and k, v written into the paged
+ * cache (pages, page, kv_heads, head_dim) at those positions' slots (block_table). bfloat16 (sc_rope_cache) or
+ * bfloat16 / float16 (sc_add_rmsnorm). */
+SC_API int sc_add_rmsnorm(void* x, const void* delta, const void* w, int rows, int cols, float eps, int dtype, void* out,
+                          void* stream);
+SC_API int sc_rope_cache(void* q, const void* k, const void* v, int tokens, int q_heads, int kv_heads, int head_dim,
+                         const float* cos, const float* sin, const int32_t* pos, const int32_t* block_table, int page,
+                         void* k_cache, void* v_cache, int dtype, void* stream);
+
 /* No counterpart in strata-mlx: an addition for callers that cannot allocate device memory.
  *
  * sc_moe_decode_layer without a workspace argument. Some hosts of this library own every byte of device memory

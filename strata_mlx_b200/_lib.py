@@ -70,6 +70,8 @@ SIGNATURES = {
     "sc_moe_decode_chain_routes": (_I, [_P, _I, _I, ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
     "sc_paged_attention": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _P, _P, _SZ, _P]),
     "sc_paged_attention_workspace": (_SZ, [_I, _I]),
+    "sc_add_rmsnorm": (_I, [_P, _P, _P, _I, _I, ctypes.c_float, _I, _P, _P]),
+    "sc_rope_cache": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P, _I, _P]),
     "sc_moe_decode_layer_noalloc": (_I, [_P, _P, _I, _P, _P]),
     "sc_moe_decode_noalloc_error": (_I, [ctypes.POINTER(_I), _P]),
 }

@@ -3,8 +3,9 @@
 // held in pages of 16 tokens. Not the hot path of this library -- the MoE expert products are -- but the decoder
 // needs it at 8K and 128K contexts, where reading the cache once is what the pass costs.
 //
-//   sc_paged_attention  flash-decoding: the context is cut into chunks of 256 keys (16 pages); a block per (chunk,
-//                       key/value head) takes the 8 query heads of its group times the window as up to 64 rows,
+//   sc_paged_attention  flash-decoding: the context is cut into about 148 chunks a key/value head (whole pages, so
+//                       that every SM has a block at 8K and 128K alike); a block per (chunk, key/value head) takes
+//                       the 8 query heads of its group times the window as up to 64 rows,
 //                       streams the chunk's pages through shared memory (cp.async, three stages), and keeps an online
 //                       softmax: scores and the value product on mma.sync (bf16, f32 sums), probabilities rounded
 //                       to bf16 for the value product. A second kernel merges the chunks' partial results.
@@ -21,7 +22,6 @@ namespace at {
 
 constexpr int D = 256;         // head dimension
 constexpr int PAGE = 16;       // tokens a page
-constexpr int CHUNK = 256;     // keys a block
 constexpr int GQA = 8;         // query heads a key/value head (16 / 2)
 constexpr int MAXROWS = 64;    // GQA x 8 tokens
 constexpr int WARPS = 8;       // warp w: query tile w / 2 (16 rows), dimension half w % 2 (128 dims)
@@ -34,6 +34,7 @@ struct Args {
   const int32_t* table;            // the sequence's pages
   const int32_t* ctx_dev;          // tokens in the cache, read on the device
   int Tq, Hq, Hkv, chunks;         // chunks: of the largest context the call allows
+  int cpages;                      // pages a chunk
   float scale_log2;                // softmax scale times log2(e)
   float* opart;                    // (chunks, Hkv, MAXROWS, D) unnormalized outputs
   float* mpart;                    // (chunks, Hkv, MAXROWS) running maxima (log2 domain)
@@ -59,7 +60,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
-__host__ __device__ inline int chunks_of(int ctx) { return (ctx + CHUNK - 1) / CHUNK; }
 
 __global__ void __launch_bounds__(WARPS * 32) attn_kernel(const Args A) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(WARPS * 32) attn_kernel(const Args A) {
   const int chunk = blockIdx.x, hk = blockIdx.y;
   const int rows = GQA * A.Tq, mtiles = (rows + 15) / 16;
   const int ctx = *A.ctx_dev;
-  const int k0 = chunk * CHUNK, k1 = min(ctx, k0 + CHUNK), pages = k1 > k0 ? (k1 - k0 + PAGE - 1) / PAGE : 0;
+  const int k0 = chunk * A.cpages * PAGE, k1 = min(ctx, k0 + A.cpages * PAGE);
+  const int pages = k1 > k0 ? (k1 - k0 + PAGE - 1) / PAGE : 0;
   // Q rows: row r = token (r / GQA), query head hk * GQA + r % GQA
   for (int i = tid; i < MAXROWS * (D / 8); i += blockDim.x) {
     const int r = i / (D / 8), c = (i % (D / 8)) * 8;
@@ -196,22 +197,51 @@ __global__ void __launch_bounds__(WARPS * 32) attn_kernel(const Args A) {
   }
 }
 
-// out[token, head, d] = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c over the chunks c
-__global__ void merge_kernel(const Args A) {
-  const int row = blockIdx.x, hk = blockIdx.y, d = threadIdx.x;  // blockDim D
+// out[token, head, d] = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c over the chunks c: a block per (row, head),
+// four groups of 256 threads (a dimension each) taking every fourth chunk, so that many loads are in flight
+constexpr int MERGE_GROUPS = 4;
+
+__global__ void __launch_bounds__(MERGE_GROUPS * D) merge_kernel(const Args A) {
+  __shared__ float s_w[1024], s_num[MERGE_GROUPS][D], s_den[MERGE_GROUPS];
+  const int row = blockIdx.x, hk = blockIdx.y, d = threadIdx.x % D, grp = threadIdx.x / D;
   const int rows = GQA * A.Tq;
   if (row >= rows) return;
-  const int chunks = min(A.chunks, chunks_of(*A.ctx_dev));  // the blocks past the context wrote nothing
+  const int ctx = *A.ctx_dev;
+  const int chunks = min(A.chunks, (ctx + A.cpages * PAGE - 1) / (A.cpages * PAGE));  // later blocks wrote nothing
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) s_w[c] = A.mpart[(int64_t(c) * A.Hkv + hk) * MAXROWS + row];
+  __syncthreads();
   float M = -1e30f;
-  for (int c = 0; c < chunks; ++c) M = fmaxf(M, A.mpart[(int64_t(c) * A.Hkv + hk) * MAXROWS + row]);
+  for (int c = 0; c < chunks; ++c) M = fmaxf(M, s_w[c]);  // a broadcast read of shared memory
+  __syncthreads();
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) s_w[c] = exp2f(s_w[c] - M);
+  __syncthreads();
   float num = 0.f, den = 0.f;
-  for (int c = 0; c < chunks; ++c) {
+#pragma unroll 8
+  for (int c = grp; c < chunks; c += MERGE_GROUPS) {
     const int64_t b = (int64_t(c) * A.Hkv + hk) * MAXROWS + row;
-    const float w = exp2f(A.mpart[b] - M);
-    num += w * A.opart[b * D + d];
-    den += w * A.lpart[b];
+    num += s_w[c] * A.opart[b * D + d];
+    den += s_w[c] * A.lpart[b];
   }
-  A.out[(int64_t(row / GQA) * A.Hq + hk * GQA + row % GQA) * D + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+  s_num[grp][d] = num;
+  if (d == 0) s_den[grp] = den;
+  __syncthreads();
+  if (grp == 0) {
+    float n = 0.f, dd = 0.f;
+#pragma unroll
+    for (int g = 0; g < MERGE_GROUPS; ++g) {
+      n += s_num[g][d];
+      dd += s_den[g];
+    }
+    A.out[(int64_t(row / GQA) * A.Hq + hk * GQA + row % GQA) * D + d] = __float2bfloat16_rn(dd > 0.f ? n / dd : 0.f);
+  }
+}
+
+// chunks of whole pages: about 148 a head (one block an SM over the heads' grid), at most 1024
+inline void chunking(int max_ctx, int kv_heads, int& cpages, int& chunks) {
+  const int pages = (max_ctx + PAGE - 1) / PAGE;
+  const int want = std::max(1, (2 * 148 + kv_heads - 1) / kv_heads);
+  cpages = std::max(1, (pages + want - 1) / want);
+  chunks = (pages + cpages - 1) / cpages;
 }
 
 }  // namespace at
@@ -221,7 +251,9 @@ using namespace sc;
 
 extern "C" size_t sc_paged_attention_workspace(int ctx, int kv_heads) {
   if (ctx < 1 || kv_heads < 1) return 0;
-  const size_t n = size_t(at::chunks_of(ctx)) * size_t(kv_heads) * at::MAXROWS;
+  int cpages, chunks;
+  at::chunking(ctx, kv_heads, cpages, chunks);
+  const size_t n = size_t(chunks) * size_t(kv_heads) * at::MAXROWS;
   return n * at::D * 4 + 2 * n * 4 + 256;
 }
 
@@ -246,7 +278,8 @@ extern "C" int sc_paged_attention(const void* q, const void* k_cache, const void
   A.Tq = tokens;
   A.Hq = q_heads;
   A.Hkv = kv_heads;
-  A.chunks = at::chunks_of(ctx);
+  at::chunking(ctx, kv_heads, A.cpages, A.chunks);
+  if (A.chunks > 1024) return SC_ERR_SHAPE;
   A.scale_log2 = scale * 1.4426950408889634f;
   const size_t n = size_t(A.chunks) * size_t(kv_heads) * at::MAXROWS;
   A.opart = static_cast<float*>(workspace);
@@ -257,7 +290,7 @@ extern "C" int sc_paged_attention(const void* q, const void* k_cache, const void
   if (int rc = raise_smem(reinterpret_cast<const void*>(at::attn_kernel), smem, "attention smem attribute")) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   at::attn_kernel<<<dim3(A.chunks, kv_heads), at::WARPS * 32, smem, s>>>(A);
-  at::merge_kernel<<<dim3(at::GQA * tokens, kv_heads), at::D, 0, s>>>(A);
+  at::merge_kernel<<<dim3(at::GQA * tokens, kv_heads), at::MERGE_GROUPS * at::D, 0, s>>>(A);
   if (cudaError_t e = cudaGetLastError()) return cuda_failed(e, "attention launch");
   return SC_OK;
 }

@@ -41,6 +41,15 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
 
 
+def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor | None, w: torch.Tensor, out: torch.Tensor,
+                eps: float = 1e-6) -> torch.Tensor:
+    """x += delta (rounded to x's type; skipped for None), out = rmsnorm(x) w: one kernel (sc_add_rmsnorm)."""
+    rows, cols = x.shape
+    check(_lib.lib().sc_add_rmsnorm(ptr(x), ptr(delta), ptr(w), rows, cols, eps, _lib.DTYPES[x.dtype], ptr(out),
+                                    stream()), "sc_add_rmsnorm")
+    return out
+
+
 class PagedCache:
     """Keys and values of one sequence for every layer, in pages of PAGE tokens: k, v (layers, pages, PAGE, kv_heads,
     HEAD_DIM) bfloat16; `table` the sequence's pages in order (a shuffled list: a sequence's pages need not be
@@ -114,6 +123,16 @@ class Dense:
         else:
             raise ValueError(f"dense kind {kind}")
 
+    @staticmethod
+    def stacked(parts: list) -> "Dense":
+        """One projection whose outputs are the parts' outputs in turn."""
+        d = Dense.__new__(Dense)
+        d.kind, d.in_f = parts[0].kind, parts[0].in_f
+        d.out_f = sum(p.out_f for p in parts)
+        d.w = torch.cat([p.w for p in parts], 0)
+        d.nbytes = sum(p.nbytes for p in parts)
+        return d
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         if self.kind == "bf16":
             return x @ self.w.T
@@ -136,24 +155,27 @@ class Attention:
         self.wk = Dense(kv_heads * HEAD_DIM, hidden, dense, gen, device)
         self.wv = Dense(kv_heads * HEAD_DIM, hidden, dense, gen, device)
         self.wo = Dense(hidden, q_heads * HEAD_DIM, dense, gen, device)
+        # q, k and v in one product: their rows stacked (blocks stay whole rows, so the bytes are concatenated)
+        self.wqkv = Dense.stacked([self.wq, self.wk, self.wv])
         self.nbytes = sum(d.nbytes for d in (self.wq, self.wk, self.wv, self.wo))
 
     def __call__(self, h: torch.Tensor, cache: PagedCache, layer: int, rope: Rope, ws: torch.Tensor,
-                 positions: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
+                 ctx: torch.Tensor) -> torch.Tensor:
         t = h.shape[0]
-        q = rope(self.wq(h).reshape(t, self.hq, HEAD_DIM), positions).contiguous()
-        k = rope(self.wk(h).reshape(t, self.hkv, HEAD_DIM), positions)
-        v = self.wv(h).reshape(t, self.hkv, HEAD_DIM)
-        kf = cache.k[layer].view(-1, self.hkv, HEAD_DIM)
-        vf = cache.v[layer].view(-1, self.hkv, HEAD_DIM)
-        kf.index_copy_(0, slots, k)
-        vf.index_copy_(0, slots, v)
+        qkv = self.wqkv(h)
+        nq, nk = self.hq * HEAD_DIM, self.hkv * HEAD_DIM
+        q = qkv[:, :nq].contiguous()
+        k = qkv[:, nq : nq + nk].contiguous()
+        v = qkv[:, nq + nk :].contiguous()
+        lib = _lib.lib()
+        # RoPE on q (in place) and k, k and v into the cache at the positions pos .. pos + t - 1
+        check(lib.sc_rope_cache(ptr(q), ptr(k), ptr(v), t, self.hq, self.hkv, HEAD_DIM, ptr(rope.cos), ptr(rope.sin),
+                                ptr(cache.pos), ptr(cache.table), PAGE, ptr(cache.k[layer]), ptr(cache.v[layer]),
+                                _lib.DTYPES[h.dtype], stream()), "sc_rope_cache")
         out = torch.empty((t, self.hq, HEAD_DIM), dtype=h.dtype, device=h.device)
-        ctx = cache.pos + t  # the window's keys are in the cache
-        check(_lib.lib().sc_paged_attention(ptr(q), ptr(cache.k[layer]), ptr(cache.v[layer]), ptr(cache.table),
-                                            ptr(ctx), cache.max_tokens, t, self.hq, self.hkv, HEAD_DIM,
-                                            1.0 / math.sqrt(HEAD_DIM), ptr(out), ptr(ws), ws.numel(), stream()),
-              "sc_paged_attention")
+        check(lib.sc_paged_attention(ptr(q), ptr(cache.k[layer]), ptr(cache.v[layer]), ptr(cache.table), ptr(ctx),
+                                     cache.max_tokens, t, self.hq, self.hkv, HEAD_DIM, 1.0 / math.sqrt(HEAD_DIM),
+                                     ptr(out), ptr(ws), ws.numel(), stream()), "sc_paged_attention")
         return self.wo(out.reshape(t, self.hq * HEAD_DIM))
 
 
@@ -274,18 +296,21 @@ class SyntheticDecoder:
         move the position (advance does), so that a verify pass can be replayed at the same place."""
         t = tokens.shape[0]
         ws = self.workspace(cache)
-        positions = cache.pos.long() + torch.arange(t, device=self.device)
-        slots = cache.slots(t)
-        x = self.embed.index_select(0, tokens)
+        ctx = cache.pos + t  # the window's keys are in the cache when attention reads it
+        x = self.embed.index_select(0, tokens)  # the residual stream, added to in place
+        h = torch.empty_like(x)
+        delta = None
         for l, L in enumerate(self.layers):
+            add_rmsnorm(x, delta, L["n1"], h)  # the previous layer's MoE output joins the stream here
             if trace is not None:
                 trace.append(x.clone())  # each layer's input, for tests that check a layer at a time
-            h = rmsnorm(x, L["n1"])
-            x = x + L["attn"](h, cache, l, self.rope, ws, positions, slots)
-            x = x + L["moe"](rmsnorm(x, L["n2"]))
+            a = L["attn"](h, cache, l, self.rope, ws, ctx)
+            add_rmsnorm(x, a, L["n2"], h)
+            delta = L["moe"](h)
+        add_rmsnorm(x, delta, self.final_norm, h)
         if trace is not None:
             trace.append(x.clone())
-        return rmsnorm(x, self.final_norm).float() @ self.head_f32.T
+        return h.float() @ self.head_f32.T
 
     @staticmethod
     def advance(cache: PagedCache, t: int) -> None:
