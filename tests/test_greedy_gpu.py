@@ -56,21 +56,37 @@ def next_token(head, x):
 
 
 def test_256_greedy_tokens_match_the_oracle(cuda):
+    """Both paths decode 256 tokens greedily, each from its own previous choice. A layer is compared after every
+    step; where a token's routes differ between the two (a one-unit difference of an activation upstream moves the
+    10th and 11th router logits past each other), the oracle's gap between its K-th and (K+1)-th logit must be a
+    near-tie (below 1e-3 of the logits' scale) and the oracle then continues from the GPU's activations (teacher
+    forcing at that layer); such re-syncs must be rare. Every step's token must be the oracle's."""
     emb, head, layers = model()
     tok_gpu = tok_ref = 1
-    same_x = 0
+    same_x, resyncs = 0, 0
     for step in range(STEPS):
         xg = dev(emb[tok_gpu][None]).to(torch.bfloat16)
         xr = emb[tok_ref][None].astype(np.float32)
         for L, W, cuda in layers:
+            xin = xg
             xg = (xg.float() + cuda(xg).float()).to(torch.bfloat16)
-            y, _, _ = R.moe_layer(xr, L["router"], L["shared_gate"], W["gate"], W["up"], W["down"], W["sgate"],
-                                  W["sup"], W["sdown"], K, "bfloat16")
-            xr = R.round_to(xr + y, "bfloat16")
+            y, idx, _ = R.moe_layer(xr, L["router"], L["shared_gate"], W["gate"], W["up"], W["down"], W["sgate"],
+                                    W["sup"], W["sdown"], K, "bfloat16")
+            xr_next = R.round_to(xr + y, "bfloat16")
+            gidx = cuda.routes(1, xin.device)[0].view(torch.int32).cpu().numpy()
+            if not np.array_equal(np.sort(gidx, -1), np.sort(idx.astype(np.int32), -1)):
+                lg = np.sort(R.router(L["router"], R.round_to(xr, "bfloat16")).reshape(-1))[::-1]
+                gap = lg[K - 1] - lg[K]
+                assert gap <= 1e-3 * np.abs(lg).max(), f"step {step}: other routes without a near-tie ({gap})"
+                resyncs += 1
+                xr_next = xg.float().cpu().numpy()
+            xr = xr_next
+            xh = xg.float().cpu().numpy()
+            assert np.isfinite(xh).all() and np.isfinite(xr).all()
+            assert np.abs(xh - xr).max() <= 2.0 ** -5 * max(1.0, np.abs(xr).max()), f"step {step}"
         xg_host = xg.float().cpu().numpy()
-        assert np.isfinite(xg_host).all() and np.isfinite(xr).all()
         same_x += int(np.array_equal(xg_host, xr))
-        assert np.abs(xg_host - xr).max() <= 2.0 ** -5 * max(1.0, np.abs(xr).max())
         tok_gpu, tok_ref = next_token(head, xg_host), next_token(head, xr)
         assert tok_gpu == tok_ref, f"step {step}: the CUDA path chose {tok_gpu}, the oracle {tok_ref}"
+    assert resyncs <= 0.05 * STEPS * LAYERS, resyncs
     assert same_x >= 0.5 * STEPS, same_x
