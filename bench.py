@@ -932,6 +932,34 @@ def step_seconds(per_layer: dict, n_layers: int, mode: str) -> float:
     return sum(per_layer[kind_of(l, mode)] for l in range(n_layers))
 
 
+def run_chain(args) -> None:
+    """--workload chain: the persistent chain kernel alone (sc_moe_decode_chain over --layers layers at --tokens
+    tokens, each layer taking the previous one's output, the window fed again every two layers), for timing and
+    profiling it; one JSON line. With --no-graph the launches are eager, as a profiler wants them."""
+    from strata_mlx_b200 import _lib
+    from strata_mlx_b200 import fused as F
+
+    _lib.load()
+    device = torch.device("cuda", torch.cuda.current_device())
+    layers = build_layers(args.layers, args.kinds, 0, device)
+    chain = F.DecodeChain(layers, EP_REFEED if args.layers % EP_REFEED == 0 else 0)
+    x = torch.randn((args.tokens, H), device=device).to(torch.bfloat16)
+    for _ in range(args.warmup):
+        chain(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        chain(x)
+    e1.record()
+    torch.cuda.synchronize()
+    chain.check_errors()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"workload": "the persistent chain kernel alone", "layers": args.layers, "tokens": args.tokens,
+                      "ms_per_launch": ms, "us_per_layer": ms * 1000 / args.layers,
+                      "tok_per_s": args.tokens / (ms * 1e-3)}), flush=True)
+
+
 def run_reference(args, world, rank) -> None:
     """--impl reference: the C oracle (the reference's block decode and MoE block restated in C) on all host
     cores, rank 0 only; each step a bounded sample of the 48-layer chain."""
@@ -996,8 +1024,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--kinds", default="mixed", choices=["mixed", "Q2_0", "IQ3_S"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "chain"],
+                    help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU); chain: the "
+                         "persistent chain kernel alone (one GPU, for profiling)")
+    ap.add_argument("--tokens", type=int, default=1, help="--workload chain: the window's tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config5-steps", type=int, default=256, help="greedy decode steps of the configuration-5 line")
     ap.add_argument("--no-extra", action="store_true",
@@ -1016,6 +1046,15 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
+    if args.workload == "chain":
+        if rank == 0:
+            run_chain(args)
+        if world > 1:
+            import torch.distributed as dist
+
+            barrier(world)
+            dist.destroy_process_group()
+        return
     if args.workload == "prefill":
         if rank == 0:
             run_prefill(args, world, rank)
