@@ -12,11 +12,12 @@ import torch
 from oracle import blocks_ref as R
 from strata_mlx_b200 import blocks as B
 from strata_mlx_b200 import fused as F
-from strata_mlx_b200.synthetic import layer_numpy
+from strata_mlx_b200.synthetic import blocks_numpy, layer_numpy
 
 pytestmark = pytest.mark.gpu
 
 V, H, I, E, K, S, LAYERS, STEPS = 512, 2048, 256, 32, 4, 256, 4, 256  # H 2048: rows of every type end on 16 bytes (the fused path)
+SIGMA = {"Q2_0": 0.02, "IQ3_S": 2e-4, "IQ3_XXS": 2e-4}
 KINDS = [("Q2_0", "Q2_0", "Q2_0"), ("IQ3_S", "IQ3_S", "IQ3_S"), ("IQ3_XXS", "IQ3_XXS", "IQ3_XXS"),
          ("IQ3_S", "IQ3_S", "Q2_0")]
 
@@ -32,11 +33,14 @@ def model(seed=7):
     layers = []
     for l in range(LAYERS):
         kinds = KINDS[l % len(KINDS)]
-        # expert scales of 6e-4: a block adds ~0.3 to a residual stream of ~4 (the benchmark's 0.02 multiplies the
-        # stream each layer and overflows); the router and shared gate keep 0.02, so that the top-k is no near-tie
-        L = layer_numpy(rng, H, I, E, kinds, shared_inter=S, sigma=6e-4)
-        L["router"] = rng.normal(0, 0.02, (E, H)).astype(np.float16)
-        L["shared_gate"] = rng.normal(0, 0.02, (H,)).astype(np.float16)
+        # expert scales by block type that make a block add O(1) to a residual stream of ~4 (an IQ3 block's output
+        # grows as its scale cubed, Q2_0's as well, from different constants): without norms between the blocks,
+        # larger scales make each block multiply the stream, and a one-unit rounding difference with it; the router
+        # and shared gate keep 0.02
+        L = layer_numpy(rng, H, I, E, kinds, shared_inter=S, sigma=0.02)
+        for name, kind, mats, r, c in (("gate", kinds[0], E, I, H), ("up", kinds[1], E, I, H), ("down", kinds[2], E, H, I),
+                                       ("sgate", kinds[0], 1, S, H), ("sup", kinds[1], 1, S, H), ("sdown", kinds[2], 1, H, S)):
+            L[name] = blocks_numpy(kind, mats, r, c, rng, SIGMA[kind])
         W = {k: R.dequantize(L[k], kind, shp) for k, kind, shp in (
             ("gate", kinds[0], (E, I, H)), ("up", kinds[1], (E, I, H)), ("down", kinds[2], (E, H, I)),
             ("sgate", kinds[0], (S, H)), ("sup", kinds[1], (S, H)), ("sdown", kinds[2], (H, S)))}
