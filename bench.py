@@ -611,6 +611,58 @@ def prefill_cpu_sample(pairs: int, flops: float, seconds: float = 10.0) -> dict:
             "sample": f"{n} pairs' gate, up and down products timed (~{seconds:.0f} s), scaled to {pairs} pairs"}
 
 
+# ---- the reference's unfused call at a mid-size batch
+
+MB_TOKENS, MB_LAYERS = 64, 3
+
+
+def mid_batch_result(reps: int = 10, layers: int = MB_LAYERS) -> dict:
+    """The reference's unfused expert call for a mid-size batch: blocks.switch_glu of 64 tokens x top-10 of 512
+    experts (config-2 shapes: gate / up 2048 -> 512, down 512 -> 2048), bfloat16 x -- the gate/up product with
+    swiglu (sc_expert_gate_up) and the down product (sc_expert_matvec), both on the grouped fragment kernel. Three
+    layers' stacks of each block type with seeded uniform routes are called in turn from a CUDA graph (a call's
+    distinct experts are ~0.4-0.5 GB of blocks: more than L2). Bytes per call: the distinct experts' gate, up and
+    down rows."""
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200.synthetic import blocks_cuda
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    pk = peaks()
+    out = {"workload": f"{MB_TOKENS} tokens x top-{K} of {E} experts (gate/up {H}->{I}, down {I}->{H}), bfloat16 x, "
+                       "through blocks.switch_glu (BlockSwitchLinear products)", "api": "strata_mlx_b200.blocks.switch_glu",
+           "gpu_launches_per_call": 2}
+    for kind in ("Q2_0", "IQ3_S"):
+        rng = np.random.default_rng(5)
+        calls, nbytes = [], []
+        for l in range(layers):
+            gate = B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, 60 + 3 * l, device), kind, (E, I, H))
+            up = B.BlockSwitchLinear(blocks_cuda(kind, E, I, H, 61 + 3 * l, device), kind, (E, I, H))
+            down = B.BlockSwitchLinear(blocks_cuda(kind, E, H, I, 62 + 3 * l, device), kind, (E, H, I))
+            idx = np.stack([rng.choice(E, K, replace=False) for _ in range(MB_TOKENS)]).astype(np.int32)
+            x = torch.from_numpy(rng.standard_normal((MB_TOKENS, H)).astype(np.float32)).to(device, torch.bfloat16)
+            calls.append((x, torch.from_numpy(idx).to(device), up, gate, down))
+            used = len(np.unique(idx))
+            nbytes.append(used * (2 * I * row_bytes(kind, H) + H * row_bytes(kind, I)))
+        g, _ = graph_of(lambda: [B.switch_glu(*c) for c in calls], device)
+        st = torch.cuda.Stream(device=device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            g.replay()
+            e0.record(st)
+            for _ in range(reps):
+                g.replay()
+            e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * layers)
+        gbs = float(np.mean(nbytes)) / (us * 1e-6) / 1e9
+        out[kind] = {"us_per_call": us, "bytes_per_call": float(np.mean(nbytes)), "gbs": gbs,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                  "frac": gbs / pk["hbm_gbs"], "peak_source": pk["source"]}}
+        del g, calls
+        torch.cuda.synchronize()
+    return out
+
+
 # ---- configurations 4 and 5 (BASELINE configs[3], configs[4]): the synthetic decoder around the MoE blocks
 
 
@@ -1024,9 +1076,10 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--kinds", default="mixed", choices=["mixed", "Q2_0", "IQ3_S"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "chain"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "chain", "mid"],
                     help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU); chain: the "
-                         "persistent chain kernel alone (one GPU, for profiling)")
+                         "persistent chain kernel alone (one GPU, for profiling); mid: the mid_batch sub-line alone "
+                         "(--steps replays, min(--layers, 3) layers a block type)")
     ap.add_argument("--tokens", type=int, default=1, help="--workload chain: the window's tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config5-steps", type=int, default=256, help="greedy decode steps of the configuration-5 line")
@@ -1046,6 +1099,19 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
+    if args.workload == "mid":
+        if rank == 0:
+            from strata_mlx_b200 import _lib
+
+            _lib.load()
+            print(json.dumps({"workload": "mid", **mid_batch_result(reps=args.steps, layers=min(args.layers, MB_LAYERS))}),
+                  flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            barrier(world)
+            dist.destroy_process_group()
+        return
     if args.workload == "chain":
         if rank == 0:
             run_chain(args)
@@ -1151,6 +1217,7 @@ def main() -> None:
         del graph
         torch.cuda.synchronize()
         line["config1"] = config1_result(cpu_seconds=None if args.no_cpu_baseline else 5.0)
+        line["mid_batch"] = mid_batch_result()
         line["prefill"] = prefill_result(20, 5, None if args.no_cpu_baseline else 6.0)
         line["config4"] = config4_result(world, rank, device)
         line["config5"] = config5_result(world, rank, device, steps=args.config5_steps)

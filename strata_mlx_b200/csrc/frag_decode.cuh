@@ -68,6 +68,29 @@ __device__ __forceinline__ const uint2* grid_tab(const uint2* tabs) {
   return KIND == SC_IQ3_XXS ? tabs + 512 : tabs;
 }
 
+// One kind's codebook in REP copies, entry i of copy c at i * REP + c: a lane that reads copy lane % REP from
+// rep_tab(tab, lane) finds its entry in its own pair of banks (REP = 16: a warp's eight-byte loads take the two
+// passes they must, whatever the entries). REP * entries * 8 bytes.
+template <int KIND> constexpr int grid_entries() { return KIND == SC_IQ3_XXS ? 256 : 512; }
+
+template <typename T, int KIND, int REP>
+__device__ __forceinline__ void build_grid_tab_rep(uint2* tab, int tid, int nthreads) {
+  for (int i = tid; i < grid_entries<KIND>() * REP; i += nthreads) {
+    const int e = i / REP;
+    const uint32_t g = KIND == SC_IQ3_XXS ? IQ3XXS_GRID[e] : IQ3S_GRID[e];
+    const T v0 = from_f32<T>(float(g & 255)), v1 = from_f32<T>(float((g >> 8) & 255));
+    const T v2 = from_f32<T>(float((g >> 16) & 255)), v3 = from_f32<T>(float(g >> 24));
+    uint2 w;
+    w.x = uint32_t(*reinterpret_cast<const uint16_t*>(&v0)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&v1)) << 16);
+    w.y = uint32_t(*reinterpret_cast<const uint16_t*>(&v2)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&v3)) << 16);
+    tab[i] = w;
+  }
+}
+template <int REP>
+__device__ __forceinline__ const uint2* rep_tab(const uint2* tab, int lane) {
+  return tab + (lane % REP);
+}
+
 // Q2_0's biases: pair q's codes at bits 2q of each half (pair 3 shifted down 4 bits first), the exponent making one
 // unit of the mantissa there 1; -(B + 1) as a pair of T, exact.
 template <typename T> struct Q2;
@@ -106,8 +129,9 @@ __device__ __forceinline__ uint32_t signs_of(uint32_t s8, int r) {
 
 // acc (the C fragment: rows g, g + 8; tokens 2t, 2t + 1) += the product of rows ra (row g) and rb (row g + 8) over
 // runs [n0, n1) (n0, n1 multiples of 4) with the activations at xg (the lane's token row g of the staged window, in
-// the kind's order; nullptr when row g is not a token of this tile, which then multiplies zeros).
-template <int KIND, typename T>
+// the kind's order, in shared or global memory; nullptr when row g is not a token of this tile, which then
+// multiplies zeros). With REP > 1, tab is the lane's copy of a codebook in REP copies (rep_tab).
+template <int KIND, typename T, int REP = 1>
 __device__ __forceinline__ void frag_runs(const uint8_t* ra, const uint8_t* rb, const T* xg, int n0, int n1, int lane,
                                           const uint2* tab, float (&acc)[4]) {
   const int t = lane & 3;
@@ -184,7 +208,7 @@ __device__ __forceinline__ void frag_runs(const uint8_t* ra, const uint8_t* rb, 
             ia = qs & 0xffu;
             ib2 = qs >> 8;
           }
-          const uint2 ga = tab[ia], gb = tab[ib2];
+          const uint2 ga = tab[ia * REP], gb = tab[ib2 * REP];
           p[0] = ga.x ^ signs_of(s8, 0);
           p[1] = ga.y ^ signs_of(s8, 1);
           p[2] = gb.x ^ signs_of(s8, 2);
@@ -206,13 +230,13 @@ __device__ __forceinline__ void frag_runs(const uint8_t* ra, const uint8_t* rb, 
 
 // Two products against the same activations at once (a gate/up item's gate rows and up rows), each run's decodes of
 // both interleaved: the same sums, in the same order, as two frag_runs calls.
-template <int KIND, typename T>
+template <int KIND, typename T, int REP = 1>
 __device__ __forceinline__ void frag_runs2(const uint8_t* ga, const uint8_t* gb, const uint8_t* ua, const uint8_t* ub,
                                            const T* xg, int n0, int n1, int lane, const uint2* tab,
                                            float (&accg)[4], float (&accu)[4]) {
   for (int n = n0; n < n1; n += 4) {
-    frag_runs<KIND, T>(ga, gb, xg, n, n + 4, lane, tab, accg);
-    frag_runs<KIND, T>(ua, ub, xg, n, n + 4, lane, tab, accu);
+    frag_runs<KIND, T, REP>(ga, gb, xg, n, n + 4, lane, tab, accg);
+    frag_runs<KIND, T, REP>(ua, ub, xg, n, n + 4, lane, tab, accu);
   }
 }
 

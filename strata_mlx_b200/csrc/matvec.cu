@@ -5,7 +5,8 @@
 //   sc_matvec_glu          matvec_glu / lookup_down_glu (blocks.py:222-259, :740-798)
 //   sc_expert_gate_up      gate(x), up(x), swiglu of switch_glu (blocks.py:808-818), fused
 //
-// One kernel serves all of them. A block first works out which experts its pairs name (a bitmap, so each
+// With 16-bit activations, a block type with fragment decoders and gm::FROM pairs or more, the grouped fragment
+// kernel (matvec_frag.cu) takes the call. Otherwise one kernel serves all of them. A block first works out which experts its pairs name (a bitmap, so each
 // expert's blocks are read once however many pairs share it), stages the activations in shared memory as
 // float32, then splits the (expert, chunk of rows) list evenly over the grid. A producer warp streams each
 // chunk's rows into a ring of shared-memory stages with 1-D bulk copies (TMA) completing on mbarriers; eight
@@ -71,6 +72,10 @@ extern "C" int sc_expert_matvec(int kind, const void* blocks, int experts, int r
   if (!dtype_ok(dtype)) return SC_ERR_DTYPE;
   if (experts > MV_MAX_EXPERTS) return SC_ERR_SHAPE;
   if (pairs == 0) return SC_OK;
+  if (int rc = gm_matvec(kind, MV_PLAIN, dtype, blocks, nullptr, experts, rows, cols, idx, pairs, share, 0, x,
+                         nullptr, out, err, static_cast<cudaStream_t>(stream));
+      rc != GM_DECLINED)
+    return rc;
   int rc = SC_OK;
   with_kind(kind, [&](auto launch) {
     rc = mv_split(pairs, share, cols, 0, [&](int p0, int n) {
@@ -145,6 +150,10 @@ extern "C" int sc_matvec_glu(int kind, const void* blocks, int experts, int rows
   if (!dtype_ok(dtype)) return SC_ERR_DTYPE;
   if (experts > MV_MAX_EXPERTS) return SC_ERR_SHAPE;
   if (pairs == 0) return SC_OK;
+  if (int rc = gm_matvec(kind, MV_GLU_IN, dtype, blocks, nullptr, experts, rows, cols, idx, pairs, 1, glu, gate, up,
+                         out, err, static_cast<cudaStream_t>(stream));
+      rc != GM_DECLINED)
+    return rc;
   int rc = SC_OK;
   with_kind(kind, [&](auto launch) {
     rc = mv_split(pairs, 1, cols, 1, [&](int p0, int n) {
@@ -172,6 +181,10 @@ extern "C" int sc_expert_gate_up(int kind, const void* gate, const void* up, int
   if (!dtype_ok(dtype)) return SC_ERR_DTYPE;
   if (experts > MV_MAX_EXPERTS) return SC_ERR_SHAPE;
   if (pairs == 0) return SC_OK;
+  if (int rc = gm_matvec(kind, MV_GATEUP, dtype, gate, up, experts, rows, cols, idx, pairs, share, 0, x, nullptr, h,
+                         err, static_cast<cudaStream_t>(stream));
+      rc != GM_DECLINED)
+    return rc;
   int rc = SC_OK;
   with_kind(kind, [&](auto launch) {
     rc = mv_split(pairs, share, cols, 0, [&](int p0, int n) {

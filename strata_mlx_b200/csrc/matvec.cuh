@@ -82,6 +82,14 @@ __device__ __forceinline__ float swiglu_mlx(float g, float u) {
 template <int KIND>
 int mv_dispatch(MvArgs a, int mode, int dtype, int units_max, int sg_hint, cudaStream_t s);
 
+// The grouped fragment path (matvec_frag.cu): 16-bit activations, block types with fragment decoders, calls of
+// gm::FROM pairs or more. Returns SC_OK or an error when it took the call, GM_DECLINED when the call is not its
+// (the exact float32 kernel then takes it).
+constexpr int GM_DECLINED = 1;
+int gm_matvec(int kind, int mode, int dtype, const void* w, const void* w2, int experts, int rows, int cols,
+              const uint32_t* idx, int pairs, int share, int glu, const void* x, const void* x2, void* out, int* err,
+              cudaStream_t s);
+
 // silu(g) * u in float32 (the Q2_0 down table's form, strata_mlx/blocks.py:709-711)
 __device__ __forceinline__ float swiglu_f32(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
