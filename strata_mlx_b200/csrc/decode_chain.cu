@@ -374,10 +374,14 @@ __global__ void __launch_bounds__(THREADS, 1) chain_kernel(const __grid_constant
     if (tid == 0) CK_TRACE(l, 1);
     // ---- R: this block's router rows
     if (!mbar_wait(rt_full, l & 1, A.err)) s_abort = 1;
-    if (warp < r_hi - r_lo && s_abort == 0) {
-      const int row = r_lo + warp;
-      const uint4* wv = reinterpret_cast<const uint4*>(rt + warp * H * 2) + lane;
-      for (int t = 0; t < T_; ++t) {
+    // warp w takes router row w % nrows for one group of the window's tokens (groups of tpg), so that every warp
+    // has a share when the block holds fewer rows than warps
+    const int nrows = r_hi - r_lo, ngroups = nrows > 0 ? max(1, CW / nrows) : 1;
+    const int tpg = (T_ + ngroups - 1) / ngroups, rl = nrows > 0 ? warp % nrows : 0, tg = nrows > 0 ? warp / nrows : 0;
+    if (nrows > 0 && tg < ngroups && s_abort == 0) {
+      const int row = r_lo + rl;
+      const uint4* wv = reinterpret_cast<const uint4*>(rt + rl * H * 2) + lane;
+      for (int t = tg * tpg; t < min(T_, (tg + 1) * tpg); ++t) {
         const uint4* xr = reinterpret_cast<const uint4*>(xs + t * (H + 32)) + lane;
         float acc = 0.f;
         for (int c = 0; c < H / 256; ++c) {

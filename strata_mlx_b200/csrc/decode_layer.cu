@@ -170,14 +170,23 @@ struct GuSmem {
   int bar, tabs, xs, red, rows, total;
 };
 
-__host__ __device__ inline GuSmem gu_smem(int tokens, int H, int64_t rb) {
+// The codebook copies a kernel keeps of its kind (rep_tab: every lane of a half-warp its own banks); the gate/up
+// kernel holds eight (three blocks an SM still fit at one token), the down kernel sixteen
+constexpr int GU_REP = 8;
+constexpr int DN_REP = 16;
+__host__ __device__ constexpr int tab_bytes_of(int kind, int rep) {
+  return kind == SC_Q2_0 ? 0 : (kind == SC_IQ3_XXS ? 256 : 512) * rep * 8;
+}
+
+// rs: the shared-memory stride of the staged gate / up rows (their row bytes)
+__host__ __device__ inline GuSmem gu_smem(int kind, int tokens, int H, int rs) {
   GuSmem s;
   int o = 0;
   s.bar = o; o += 16;
-  s.tabs = o; o += align16(GRID_TAB_BYTES);
+  s.tabs = o; o += align16(tab_bytes_of(kind, GU_REP));
   s.xs = o; o += align16(tokens * (H + 32) * 2);
   s.red = o; o += WARPS * 32 * 8 * 4;
-  s.rows = o; o += 2 * align16(int(RG * rb));
+  s.rows = o; o += 2 * align16(RG * rs);
   s.total = o;
   return s;
 }
@@ -194,12 +203,15 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   const bool shared = u == 0;
   const int rows = shared ? min(RG, L.Is - r0) : min(RG, L.I - r0);
   const int64_t rb = shared ? L.rb_sgu : L.rb_gu;
-  const GuSmem S = gu_smem(T_, H, max(L.rb_gu, L.rb_sgu));
+  // the rows stay unpadded in shared memory: Q2_0's 576-byte rows meet four-way bank conflicts on their code loads,
+  // but padding them (a bulk copy per row, or the block's own loads) made this latency-bound kernel slower
+  const int rs = int(max(L.rb_gu, L.rb_sgu));
+  const GuSmem S = gu_smem(KIND, T_, H, rs);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S.bar);
   T* xs = reinterpret_cast<T*>(smem + S.xs);
   float* red = reinterpret_cast<float*>(smem + S.red);
   uint8_t* wg = smem + S.rows;
-  uint8_t* wu = wg + align16(int(RG * max(L.rb_gu, L.rb_sgu)));
+  uint8_t* wu = wg + align16(RG * rs);
   if (rows <= 0) {  // this block's rows lie beyond the unit's (the shared expert may be narrower)
     pdl_launch_dependents();
     return;
@@ -214,8 +226,8 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
     }
   }
   uint2* tabs = reinterpret_cast<uint2*>(smem + S.tabs);
-  if constexpr (KIND != SC_Q2_0) build_grid_tabs<T>(tabs, tid, blockDim.x);
-  const uint2* tab = grid_tab<KIND>(tabs);
+  if constexpr (KIND != SC_Q2_0) build_grid_tab_rep2<T, KIND, GU_REP>(tabs, tid, blockDim.x);
+  const uint2* tab = rep_tab<GU_REP>(tabs, lane);
   // the window's activations are complete once the route kernel let this kernel start (it waits before it does);
   // over peer memory, the window's count is read here too (already full), for the peers' writes' visibility
   if (L.peers) {
@@ -251,8 +263,8 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
   if (!mbar_wait(bar, 0, L.err)) return;
   TRACE_POINT(1, 3);
-  frag_runs2<KIND, T>(wg + g * rb, wg + (g + 8) * rb, wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane, tab, accg,
-                      accu);
+  frag_runs2<KIND, T, GU_REP>(wg + g * rs, wg + (g + 8) * rs, wu + g * rs, wu + (g + 8) * rs, xg, n0, n1, lane, tab,
+                              accg, accu);
   TRACE_POINT(1, 4);
   // red[value][warp][lane]: the reducing thread (value q, lane L) reads eight consecutive words
   red[((0 + 0) * WARPS + warp) * 32 + lane] = accg[0];
@@ -290,11 +302,11 @@ struct DnSmem {
   int bars, tabs, plan, wts, ys, stages, total;
 };
 
-__host__ __device__ inline DnSmem dn_smem(int tokens, int K, int stage_bytes, int stages) {
+__host__ __device__ inline DnSmem dn_smem(int kind, int tokens, int K, int stage_bytes, int stages) {
   DnSmem s;
   int o = 0;
   s.bars = o; o += align16(2 * MAX_STAGES * 8);
-  s.tabs = o; o += align16(GRID_TAB_BYTES);
+  s.tabs = o; o += align16(tab_bytes_of(kind, DN_REP));
   s.plan = o; o += align16(int(sizeof(Plan)));
   s.wts = o; o += align16(tokens * (K + 1) * 4);
   s.ys = o; o += align16(tokens * (K + 1) * RC * 4);
@@ -333,7 +345,8 @@ __device__ __forceinline__ void down_piece(const LayerDev& L, uint8_t* st, int h
   const int64_t rb = shared ? L.rb_sd : L.rb_d;
   const bool mine = g < T_ && ((mask >> g) & 1u);
   acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-  frag_runs<KIND, T>(st + g * rb, st + (g + 8) * rb, mine ? hs + g * L.hstride : nullptr, n0, n1, lane, tab, acc);
+  frag_runs<KIND, T, DN_REP>(st + g * rb, st + (g + 8) * rb, mine ? hs + g * L.hstride : nullptr, n0, n1, lane, tab,
+                             acc);
 }
 
 template <int KIND, typename T>
@@ -343,7 +356,7 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T_ = L.T, K = L.K, H = L.H;
-  const DnSmem S = dn_smem(T_, K, L.dn_stage, L.dn_stages);
+  const DnSmem S = dn_smem(KIND, T_, K, L.dn_stage, L.dn_stages);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S.bars);
   uint64_t* empty = full + MAX_STAGES;
   Plan* plan = reinterpret_cast<Plan*>(smem + S.plan);
@@ -361,8 +374,8 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
     fence_mbar_init();
   }
   uint2* tabs = reinterpret_cast<uint2*>(smem + S.tabs);
-  if constexpr (KIND != SC_Q2_0) build_grid_tabs<T>(tabs, tid, blockDim.x);
-  const uint2* tab = grid_tab<KIND>(tabs);
+  if constexpr (KIND != SC_Q2_0) build_grid_tab_rep2<T, KIND, DN_REP>(tabs, tid, blockDim.x);
+  const uint2* tab = rep_tab<DN_REP>(tabs, lane);
   // the routes and the plan are complete once the gate/up kernel let this kernel start (it waits before it does)
   for (int i = tid; i < int(sizeof(Plan) / 16); i += blockDim.x)
     reinterpret_cast<int4*>(plan)[i] = __ldcg(reinterpret_cast<const int4*>(L.plan) + i);
@@ -512,14 +525,15 @@ static cudaError_t launch_pdl(Kern kern, int grid, int threads, int smem, cudaSt
 template <int KGU, int KD, typename T>
 static int run(LayerDev L, cudaStream_t s, int stage) {
   const int max_units = L.T * L.K + 1;
-  const int gu_total = gu_smem(L.T, L.H, std::max(L.rb_gu, L.rb_sgu)).total;
+  const int gu_total = gu_smem(KGU, L.T, L.H, int(std::max(L.rb_gu, L.rb_sgu))).total;
   // down: a stage is one unit's 16 rows and its h; enough stages for every warp to hold one and the next in flight
   L.dn_stage = align16(RC * int(std::max(L.rb_d, L.rb_sd))) + align16(L.T * L.hstride * 2);
-  L.dn_stages = std::max(2, std::min({MAX_STAGES, max_units, (144 * 1024) / L.dn_stage}));
+  const int dn_room = std::min(144 * 1024, 227 * 1024 - dn_smem(KD, L.T, L.K, L.dn_stage, 0).total);
+  L.dn_stages = std::max(2, std::min({MAX_STAGES, max_units, dn_room / L.dn_stage}));
   if (L.dn_stages > DN_WARPS) L.dn_stages -= L.dn_stages % DN_WARPS;  // every warp the same number of stages
   // one down block an SM: two on one SM (where the gate/up blocks left room first) ran twice as long, and the
   // layer waits for the slowest; more than half an SM's shared memory keeps a second one off
-  const int dn_total = std::max(dn_smem(L.T, L.K, L.dn_stage, L.dn_stages).total, 116 * 1024);
+  const int dn_total = std::max(dn_smem(KD, L.T, L.K, L.dn_stage, L.dn_stages).total, 116 * 1024);
   if (gu_total > 227 * 1024 || dn_total > 227 * 1024) return SC_ERR_SHAPE;
 
   auto kr = L.T == 1   ? route_kernel<T, 1>

@@ -91,6 +91,25 @@ __device__ __forceinline__ const uint2* rep_tab(const uint2* tab, int lane) {
   return tab + (lane % REP);
 }
 
+// One IQ3 kind's codebook replicated REP times (rep_tab's layout), built by `nthreads` threads from `tid`: each
+// thread expands an entry once and stores it into two adjacent copies with one 16-byte store.
+template <typename T, int KIND, int REP>
+__device__ __forceinline__ void build_grid_tab_rep2(uint2* tab, int tid, int nthreads) {
+  static_assert(REP % 2 == 0, "copies are stored in pairs");
+  for (int i = tid; i < grid_entries<KIND>() * (REP / 2); i += nthreads) {
+    const int e = i / (REP / 2), c = 2 * (i % (REP / 2));
+    const uint32_t g = KIND == SC_IQ3_XXS ? IQ3XXS_GRID[e] : IQ3S_GRID[e];
+    const T v0 = from_f32<T>(float(g & 255)), v1 = from_f32<T>(float((g >> 8) & 255));
+    const T v2 = from_f32<T>(float((g >> 16) & 255)), v3 = from_f32<T>(float(g >> 24));
+    uint4 w;
+    w.x = uint32_t(*reinterpret_cast<const uint16_t*>(&v0)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&v1)) << 16);
+    w.y = uint32_t(*reinterpret_cast<const uint16_t*>(&v2)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&v3)) << 16);
+    w.z = w.x;
+    w.w = w.y;
+    *reinterpret_cast<uint4*>(tab + e * REP + c) = w;
+  }
+}
+
 // Q2_0's biases: pair q's codes at bits 2q of each half (pair 3 shifted down 4 bits first), the exponent making one
 // unit of the mantissa there 1; -(B + 1) as a pair of T, exact.
 template <typename T> struct Q2;
