@@ -16,6 +16,8 @@
 //
 // Block types with fragment decoders: Q2_0, IQ3_S, IQ3_XXS (HasMma); other layers take moe.cu's chain.
 #include <algorithm>
+#include <mutex>
+#include <vector>
 
 #include "matvec.cuh"
 #include "frag_decode.cuh"
@@ -85,8 +87,12 @@ template <typename T, int MT>
 __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   TRACE_POINT(0, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int row = blockIdx.x * RT_WARPS + warp;  // router rows 0 .. E-1; row E is the shared expert's gate
+  // block b: router rows of row block b % RB (warp w: row 16 (b % RB) + w; rows 0 .. E-1, row E the shared expert's
+  // gate) for token group b / RB of the window (groups of tpg tokens)
+  const int RB = int(gridDim.x) / L.rt_groups;
+  const int row = (blockIdx.x % RB) * RT_WARPS + warp, tg = blockIdx.x / RB;
   const int H = L.H, E = L.E, K = L.K, T_ = L.T;
+  const int tpg = (T_ + L.rt_groups - 1) / L.rt_groups, t0 = tg * tpg, t1 = min(T_, t0 + tpg);
   const __half* wrow = row < E ? L.router + int64_t(row) * H : (row == E && L.Is > 0 ? L.shared_gate : nullptr);
   const int chunks = H / 256;  // 16-byte chunks a lane reads
   // the first PRE chunks are fetched before the wait; more would spill at 128 registers a thread
@@ -105,13 +111,11 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
       const uint64_t own = L.peers[L.rank];
       ep::wait_count(ep::at_u32(own, ep::xcount_off(L.par)), L.xtarget, L.err);
       TRACE_POINT(0, 7);
-      // the previous layer's pair-output count: its combine has read it (it ran before this kernel's wait)
-      if (blockIdx.x == 0) *ep::at_u32(own, ep::ycount_off(L.par ^ 1)) = 0;
     }
     __syncthreads();
   }
   if (wrow) {
-    for (int t = 0; t < T_; ++t) {
+    for (int t = t0; t < t1; ++t) {
       const uint4* xr = reinterpret_cast<const uint4*>(static_cast<const T*>(L.x) + int64_t(t) * H);
       float acc = 0.f;
 #pragma unroll
@@ -157,41 +161,80 @@ __global__ void __launch_bounds__(RT_THREADS) route_kernel(LayerDev L) {
   if (tid == 0) {
     L.plan->units = units;
     *L.ticket = 0;  // ready for the next call on this workspace
+    if (L.peers) ++*L.step;  // this call's step number: the tag of its pair outputs (every rank counts alike)
     TRACE_POINT(0, 5);
   }
 }
 
 // ---------------------------------------------------------------------------------------------------- gate_up
 //
-// One block per (unit, block of 16 rows): the unit's gate and up rows [r0, r0 + 16) (one bulk copy each), eight
-// warps each taking an eighth of the columns, one reduction through shared memory at the end.
+// Items are (unit, block of 16 rows): the unit's gate and up rows [r0, r0 + 16) (one bulk copy each), eight warps
+// each taking an eighth of the columns, one reduction through shared memory at the end. When every item of the
+// largest window fits on the GPU at once (one or two tokens), a block takes one item; otherwise (LOOP) the grid is
+// as many blocks as are resident and block b takes items b, b + grid, ... of the window's units, so that the units
+// a window does not have cost nothing and the codebook is built once per block. (One kernel for both cost the
+// one-item case registers and ~1.5 us a launch.)
 
 struct GuSmem {
   int bar, tabs, xs, red, rows, total;
 };
 
 // The codebook copies a kernel keeps of its kind (rep_tab: every lane of a half-warp its own banks); the gate/up
-// kernel holds eight (three blocks an SM still fit at one token), the down kernel sixteen
+// kernel holds eight (three blocks an SM still fit at one or two tokens), the down kernel sixteen
 constexpr int GU_REP = 8;
 constexpr int DN_REP = 16;
 __host__ __device__ constexpr int tab_bytes_of(int kind, int rep) {
   return kind == SC_Q2_0 ? 0 : (kind == SC_IQ3_XXS ? 256 : 512) * rep * 8;
 }
 
-// rs: the shared-memory stride of the staged gate / up rows (their row bytes)
-__host__ __device__ inline GuSmem gu_smem(int kind, int tokens, int H, int rs) {
+// rs: the shared-memory stride of the staged gate / up rows (their row bytes). With `alias` the warps' sums take
+// the rows' space once the rows are decoded (the looping kernel), else a region of their own.
+__host__ __device__ inline GuSmem gu_smem(int kind, int tokens, int H, int rs, bool alias) {
   GuSmem s;
   int o = 0;
   s.bar = o; o += 16;
   s.tabs = o; o += align16(tab_bytes_of(kind, GU_REP));
   s.xs = o; o += align16(tokens * (H + 32) * 2);
-  s.red = o; o += WARPS * 32 * 8 * 4;
-  s.rows = o; o += 2 * align16(RG * rs);
+  const int rows_bytes = 2 * align16(RG * rs), red_bytes = WARPS * 32 * 8 * 4;
+  if (alias) {
+    s.red = s.rows = o; o += rows_bytes > red_bytes ? rows_bytes : red_bytes;
+  } else {
+    s.red = o; o += red_bytes;
+    s.rows = o; o += rows_bytes;
+  }
   s.total = o;
   return s;
 }
 
-template <int KIND, int KD, typename T>
+// The warps' sums of an item (C fragments: rows g, g + 8; tokens 2t, 2t + 1) met through shared memory `red`, in
+// warp order, and swiglu as mlx-lm rounds it -> h, in the order its consumer (the down product's decoder) wants.
+template <int KD, typename T>
+__device__ __forceinline__ void gu_store(const LayerDev& L, float* red, const float (&accg)[4], const float (&accu)[4],
+                                         int u, int r0, int rows, uint32_t tokmask, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  // red[value][warp][lane]: the reducing thread (value q, lane L) reads eight consecutive words
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    red[(q * WARPS + warp) * 32 + lane] = accg[q];
+    red[((4 + q) * WARPS + warp) * 32 + lane] = accu[q];
+  }
+  __syncthreads();
+  if (tid < 128) {
+    const int Lq = tid & 31, q = tid >> 5;
+    float sg = 0.f, su = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+      sg += red[(q * WARPS + w) * 32 + Lq];
+      su += red[((4 + q) * WARPS + w) * 32 + Lq];
+    }
+    const int m = (q < 2 ? 0 : 8) + (Lq >> 2), tok = 2 * (Lq & 3) + (q & 1);
+    if (m < rows && tok < L.T && ((tokmask >> tok) & 1u))
+      static_cast<T*>(L.h)[(int64_t(u) * L.T + tok) * L.hstride + x_col(r0 + m, x_pairs(KD))] =
+          from_f32<T>(swiglu_mlx<T>(sg, su));
+  }
+}
+
+template <int KIND, int KD, typename T, bool LOOP>
 __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   TRACE_POINT(1, 0);
   TRACE_SMID(1, 2);
@@ -199,30 +242,37 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T_ = L.T, H = L.H;
   const int nrb = int(ceil_div(max(L.I, L.Is), RG));
-  const int u = blockIdx.x / nrb, r0 = (blockIdx.x % nrb) * RG;
-  const bool shared = u == 0;
-  const int rows = shared ? min(RG, L.Is - r0) : min(RG, L.I - r0);
-  const int64_t rb = shared ? L.rb_sgu : L.rb_gu;
   // the rows stay unpadded in shared memory: Q2_0's 576-byte rows meet four-way bank conflicts on their code loads,
   // but padding them (a bulk copy per row, or the block's own loads) made this latency-bound kernel slower
   const int rs = int(max(L.rb_gu, L.rb_sgu));
-  const GuSmem S = gu_smem(KIND, T_, H, rs);
+  const GuSmem S = gu_smem(KIND, T_, H, rs, LOOP);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S.bar);
   T* xs = reinterpret_cast<T*>(smem + S.xs);
   float* red = reinterpret_cast<float*>(smem + S.red);
   uint8_t* wg = smem + S.rows;
   uint8_t* wu = wg + align16(RG * rs);
-  if (rows <= 0) {  // this block's rows lie beyond the unit's (the shared expert may be narrower)
-    pdl_launch_dependents();
-    return;
+  auto rows_of = [&](int j, int& u, int& r0) {
+    u = j / nrb;
+    r0 = (j % nrb) * RG;
+    return u == 0 ? min(RG, L.Is - r0) : min(RG, L.I - r0);
+  };
+  // the block's first item; if it is the shared expert's (unit 0 is in every window), its rows come before the wait
+  int u0, r00;
+  const int rows0 = rows_of(blockIdx.x, u0, r00);
+  if constexpr (!LOOP) {
+    if (rows0 <= 0) {  // this block's rows lie beyond the unit's (the shared expert may be narrower)
+      pdl_launch_dependents();
+      return;
+    }
   }
+  const bool prefetched = u0 == 0 && rows0 > 0;
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
-    if (shared) {  // the shared expert does not wait for the routes
-      mbar_arrive_expect_tx(bar, uint32_t(2 * rows * rb));
-      bulk_load(wg, L.sgate + r0 * rb, uint32_t(rows * rb), bar);
-      bulk_load(wu, L.sup + r0 * rb, uint32_t(rows * rb), bar);
+    if (prefetched) {
+      mbar_arrive_expect_tx(bar, uint32_t(2 * rows0 * L.rb_sgu));
+      bulk_load(wg, L.sgate + r00 * L.rb_sgu, uint32_t(rows0 * L.rb_sgu), bar);
+      bulk_load(wu, L.sup + r00 * L.rb_sgu, uint32_t(rows0 * L.rb_sgu), bar);
     }
   }
   uint2* tabs = reinterpret_cast<uint2*>(smem + S.tabs);
@@ -241,54 +291,56 @@ __global__ void __launch_bounds__(WARPS * 32) gate_up_kernel(LayerDev L) {
   pdl_launch_dependents();
   __shared__ Unit s_unit;
   __shared__ int s_units;
-  if (tid == 0) {
-    s_units = __ldcg(&L.plan->units);
-    if (u < s_units) {
-      const int4 v = __ldcg(reinterpret_cast<const int4*>(&L.plan->unit[u]));
-      s_unit = Unit{v.x, uint32_t(v.y), uint32_t(v.z), 0};
-      if (!shared) {
-        const int64_t e = v.x;
-        mbar_arrive_expect_tx(bar, uint32_t(2 * rows * rb));
-        bulk_load(wg, L.gate + (e * L.I + r0) * rb, uint32_t(rows * rb), bar);
-        bulk_load(wu, L.up + (e * L.I + r0) * rb, uint32_t(rows * rb), bar);
-      }
-    }
-  }
-  __syncthreads();
-  if (u >= s_units) return;  // no such unit in this window (the grid is sized for the largest window)
-
   const int g = lane >> 2;
   const int q4 = H / 128, n0 = 4 * (warp * q4 / WARPS), n1 = 4 * ((warp + 1) * q4 / WARPS);  // runs, by fours
   const T* xg = g < T_ ? xs + g * (H + 32) : nullptr;
-  float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
-  if (!mbar_wait(bar, 0, L.err)) return;
-  TRACE_POINT(1, 3);
-  frag_runs2<KIND, T, GU_REP>(wg + g * rs, wg + (g + 8) * rs, wu + g * rs, wu + (g + 8) * rs, xg, n0, n1, lane, tab,
-                              accg, accu);
-  TRACE_POINT(1, 4);
-  // red[value][warp][lane]: the reducing thread (value q, lane L) reads eight consecutive words
-  red[((0 + 0) * WARPS + warp) * 32 + lane] = accg[0];
-  red[((0 + 1) * WARPS + warp) * 32 + lane] = accg[1];
-  red[((0 + 2) * WARPS + warp) * 32 + lane] = accg[2];
-  red[((0 + 3) * WARPS + warp) * 32 + lane] = accg[3];
-  red[((4 + 0) * WARPS + warp) * 32 + lane] = accu[0];
-  red[((4 + 1) * WARPS + warp) * 32 + lane] = accu[1];
-  red[((4 + 2) * WARPS + warp) * 32 + lane] = accu[2];
-  red[((4 + 3) * WARPS + warp) * 32 + lane] = accu[3];
-  __syncthreads();
-  if (tid < 128) {
-    const int Lq = tid & 31, q = tid >> 5;
-    float sg = 0.f, su = 0.f;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) {
-      sg += red[(q * WARPS + w) * 32 + Lq];
-      su += red[((4 + q) * WARPS + w) * 32 + Lq];
+  // tid 0: unit u's plan entry into s_unit, and the copies of its rows [r0, r0 + rows) unless already issued
+  auto fetch = [&](int u, int r0, int rows, bool issued) {
+    const int4 v = __ldcg(reinterpret_cast<const int4*>(&L.plan->unit[u]));
+    s_unit = Unit{v.x, uint32_t(v.y), uint32_t(v.z), 0};
+    if (!issued) {
+      const int64_t rb = u == 0 ? L.rb_sgu : L.rb_gu;
+      const uint8_t* g0 = u == 0 ? L.sgate + r0 * rb : L.gate + (int64_t(v.x) * L.I + r0) * rb;
+      const uint8_t* u1 = u == 0 ? L.sup + r0 * rb : L.up + (int64_t(v.x) * L.I + r0) * rb;
+      mbar_arrive_expect_tx(bar, uint32_t(2 * rows * rb));
+      bulk_load(wg, g0, uint32_t(rows * rb), bar);
+      bulk_load(wu, u1, uint32_t(rows * rb), bar);
     }
-    const int m = (q < 2 ? 0 : 8) + (Lq >> 2), tok = 2 * (Lq & 3) + (q & 1);
-    if (m < rows && tok < T_ && ((s_unit.tokmask >> tok) & 1u)) {
-      // h is stored in the order its consumer (the down product's decoder) wants
-      static_cast<T*>(L.h)[(int64_t(u) * T_ + tok) * L.hstride + x_col(r0 + m, x_pairs(KD))] =
-          from_f32<T>(swiglu_mlx<T>(sg, su));
+  };
+  if constexpr (!LOOP) {
+    if (tid == 0) {
+      s_units = __ldcg(&L.plan->units);
+      if (u0 < s_units) fetch(u0, r00, rows0, prefetched);
+    }
+    __syncthreads();
+    if (u0 >= s_units) return;  // no such unit in this window (the grid is sized for the largest window)
+    const int64_t rb = u0 == 0 ? L.rb_sgu : L.rb_gu;
+    float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+    if (!mbar_wait(bar, 0, L.err)) return;
+    TRACE_POINT(1, 3);
+    frag_runs2<KIND, T, GU_REP>(wg + g * rb, wg + (g + 8) * rb, wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane,
+                                tab, accg, accu);
+    TRACE_POINT(1, 4);
+    gu_store<KD, T>(L, red, accg, accu, u0, r00, rows0, s_unit.tokmask, tid);
+  } else {
+    int it = 0;  // items this block took: the barrier's phase
+    if (tid == 0) s_units = __ldcg(&L.plan->units);
+    for (int j = blockIdx.x;; j += gridDim.x) {
+      int u, r0;
+      const int rows = rows_of(j, u, r0);
+      if (tid == 0 && u < s_units && rows > 0) fetch(u, r0, rows, it == 0 && prefetched);
+      __syncthreads();
+      if (u >= s_units) break;  // past the window's units (the grid is sized for the largest window)
+      if (rows <= 0) continue;  // rows beyond the unit's (the shared expert may be narrower)
+      const int64_t rb = u == 0 ? L.rb_sgu : L.rb_gu;
+      float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!mbar_wait(bar, uint32_t(it & 1), L.err)) break;
+      frag_runs2<KIND, T, GU_REP>(wg + g * rb, wg + (g + 8) * rb, wu + g * rb, wu + (g + 8) * rb, xg, n0, n1, lane,
+                                  tab, accg, accu);
+      __syncthreads();  // every warp is done with the rows: their space takes the sums
+      gu_store<KD, T>(L, red, accg, accu, u, r0, rows, s_unit.tokmask, tid);
+      __syncthreads();  // the sums are read: the next item's rows may land in their space
+      ++it;
     }
   }
 }
@@ -459,25 +511,47 @@ __global__ void __launch_bounds__(DN_THREADS) down_kernel(LayerDev L) {
   TRACE_POINT(2, 3);
   named_sync(1, DN_WARPS * 32);
   TRACE_POINT(2, 4);
-  if (L.peers) {  // expert parallel over peer memory: each pair's output to its token's rank, then count there
+  if (L.peers) {  // expert parallel over peer memory: each pair's output to its token's rank, as tagged words
+    // a thread a pair (tok, k) of this rank's experts: its 16 rows [r0, r0 + 16) are eight words of the owner's Y,
+    // each tagged with this call's step; then a thread a token for the shared expert's rows (local)
     const size_t yo = ep::yoff(L.par, T_, L.tl, K, H);
-    for (int i = tid; i < T_ * RC; i += DN_WARPS * 32) {
-      const int tok = i / RC, m = i % RC;
-      const float* yk = ys + tok * (K + 1) * RC + m;
-      T* dst = reinterpret_cast<T*>(L.peers[tok / L.tl] + yo) + int64_t(tok % L.tl) * K * H + r0 + m;
-      for (int k = 0; k < K; ++k) {
-        const int e = int(__ldcg(L.idx + tok * K + k));
-        if (e >= L.e0 && e < L.e1) dst[int64_t(k) * H] = from_f32<T>(yk[k * RC]);
+    const uint32_t step = __ldcg(L.step);
+    auto pack16 = [&](const float* y, uint4 (&v)[2]) {  // 16 floats -> 16 values of T
+      uint32_t w[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const T a = from_f32<T>(y[2 * q]), b = from_f32<T>(y[2 * q + 1]);
+        w[q] = uint32_t(*reinterpret_cast<const uint16_t*>(&a)) | (uint32_t(*reinterpret_cast<const uint16_t*>(&b)) << 16);
       }
-      static_cast<T*>(L.sout)[int64_t(tok) * H + r0 + m] = from_f32<T>(L.Is > 0 ? yk[K * RC] : 0.f);
+      v[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      v[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    };
+    for (int i = tid; i < T_ * K; i += DN_WARPS * 32) {
+      const int tok = i / K, k = i % K;
+      const int e = int(__ldcg(L.idx + i));
+      if (e < L.e0 || e >= L.e1) continue;
+      uint4 v[2];
+      pack16(ys + (tok * (K + 1) + k) * RC, v);
+      uint64_t* dst = reinterpret_cast<uint64_t*>(L.peers[tok / L.tl] + yo) + (int64_t(tok % L.tl) * K + k) * (H / 2) +
+                      r0 / 2;
+      const uint32_t w[8] = {v[0].x, v[0].y, v[0].z, v[0].w, v[1].x, v[1].y, v[1].z, v[1].w};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ep::store_tagged(dst + q, w[q], step);
     }
+    for (int tok = tid; tok < T_; tok += DN_WARPS * 32) {
+      uint4 v[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if (L.Is > 0) pack16(ys + (tok * (K + 1) + K) * RC, v);
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(L.sout) + int64_t(tok) * H + r0);
+      dst[0] = v[0];
+      dst[1] = v[1];
+    }
+    // the shared expert's outputs are local: this rank's combine reads them once every block counted here
     named_sync(1, DN_WARPS * 32);
-    TRACE_POINT(2, 6);
     if (tid == 0) {
-      ep::fence_release_sys();
-      for (int g = 0; g < L.G; ++g) ep::count_relaxed(ep::at_u32(L.peers[g], ep::ycount_off(L.par)));
+      __threadfence();
+      atomicAdd(L.done, 1u);
     }
-    TRACE_POINT(2, 7);
+    TRACE_POINT(2, 6);
     return;
   }
   if (L.ypairs) {  // expert parallel: the pairs' outputs (zero for other ranks' experts) and the shared expert's
@@ -522,10 +596,33 @@ static cudaError_t launch_pdl(Kern kern, int grid, int threads, int smem, cudaSt
   return cudaLaunchKernelEx(&cfg, kern, L);
 }
 
+// Blocks of `kern` (threads, dynamic shared memory) resident at once on the current device, 0 when CUDA cannot say;
+// remembered per device, kernel and size (a launch asks for each layer)
+static int resident_blocks(const void* kern, int threads, int smem) {
+  struct Entry {
+    int dev;
+    const void* kern;
+    int threads, smem, blocks;
+  };
+  static std::mutex m;
+  static std::vector<Entry> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(m);
+  for (const Entry& e : cache)
+    if (e.dev == dev && e.kern == kern && e.threads == threads && e.smem == smem) return e.blocks;
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, size_t(smem)) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  cache.push_back(Entry{dev, kern, threads, smem, per_sm * sms});
+  return per_sm * sms;
+}
+
 template <int KGU, int KD, typename T>
 static int run(LayerDev L, cudaStream_t s, int stage) {
   const int max_units = L.T * L.K + 1;
-  const int gu_total = gu_smem(KGU, L.T, L.H, int(std::max(L.rb_gu, L.rb_sgu))).total;
+  const int gu_rs = int(std::max(L.rb_gu, L.rb_sgu));
   // down: a stage is one unit's 16 rows and its h; enough stages for every warp to hold one and the next in flight
   L.dn_stage = align16(RC * int(std::max(L.rb_d, L.rb_sd))) + align16(L.T * L.hstride * 2);
   const int dn_room = std::min(144 * 1024, 227 * 1024 - dn_smem(KD, L.T, L.K, L.dn_stage, 0).total);
@@ -534,20 +631,39 @@ static int run(LayerDev L, cudaStream_t s, int stage) {
   // one down block an SM: two on one SM (where the gate/up blocks left room first) ran twice as long, and the
   // layer waits for the slowest; more than half an SM's shared memory keeps a second one off
   const int dn_total = std::max(dn_smem(KD, L.T, L.K, L.dn_stage, L.dn_stages).total, 116 * 1024);
-  if (gu_total > 227 * 1024 || dn_total > 227 * 1024) return SC_ERR_SHAPE;
+  // gate/up: one block an item when every item of the largest window is resident at once, else looping blocks (as
+  // many as are resident), whose sums take the rows' space
+  const int gu_items = max_units * int(ceil_div(std::max(L.I, L.Is), RG));
+  const int gu_one = gu_smem(KGU, L.T, L.H, gu_rs, false).total, gu_alias = gu_smem(KGU, L.T, L.H, gu_rs, true).total;
+  if (gu_alias > 227 * 1024 || dn_total > 227 * 1024) return SC_ERR_SHAPE;
 
   auto kr = L.T == 1   ? route_kernel<T, 1>
             : L.T == 2 ? route_kernel<T, 2>
             : L.T <= 4 ? route_kernel<T, 4>
                        : route_kernel<T, MAXT>;
-  auto kg = gate_up_kernel<KGU, KD, T>;
+  auto kg1 = gate_up_kernel<KGU, KD, T, false>;
+  auto kgl = gate_up_kernel<KGU, KD, T, true>;
   auto kd = down_kernel<KD, T>;
   // the dynamic shared memory a launch may take is raised to what it needs, per kernel: the gate/up and down
   // kernels are shared by the paths of several block-type mixes, each with its own sizes
-  if (int rc = raise_smem(reinterpret_cast<const void*>(kg), gu_total, "decode gate_up smem attribute")) return rc;
+  int resident = 0;
+  if (gu_one <= 227 * 1024) {
+    if (int rc = raise_smem(reinterpret_cast<const void*>(kg1), gu_one, "decode gate_up smem attribute")) return rc;
+    resident = resident_blocks(reinterpret_cast<const void*>(kg1), WARPS * 32, gu_one);
+  }
+  const bool gu_loop = gu_items > resident;
+  const int gu_total = gu_loop ? gu_alias : gu_one;
+  auto kg = gu_loop ? kgl : kg1;
+  int grid_g = gu_items;
+  if (gu_loop) {
+    if (int rc = raise_smem(reinterpret_cast<const void*>(kgl), gu_alias, "decode gate_up smem attribute")) return rc;
+    grid_g = resident_blocks(reinterpret_cast<const void*>(kgl), WARPS * 32, gu_alias);
+    if (grid_g <= 0) return cuda_failed(cudaGetLastError(), "decode gate_up occupancy");
+  }
   if (int rc = raise_smem(reinterpret_cast<const void*>(kd), dn_total, "decode down smem attribute")) return rc;
-  const int grid_r = int(ceil_div(L.E + 1, RT_WARPS));
-  const int grid_g = max_units * int(ceil_div(std::max(L.I, L.Is), RG));
+  // route: the window's tokens in groups of two over as many groups of blocks (one token: one group)
+  L.rt_groups = (L.T + 1) / 2;
+  const int grid_r = int(ceil_div(L.E + 1, RT_WARPS)) * L.rt_groups;
   const int grid_d = L.H / RC;
   if (stage < 0 || stage == 0)
     if (cudaError_t e = launch_pdl(kr, grid_r, RT_THREADS, 0, s, L)) return cuda_failed(e, "decode route launch");
@@ -629,7 +745,8 @@ int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t*
   d.tl = ep.tl;
   d.par = ep.par;
   d.xtarget = uint32_t(ep.G * ep::COMBINE_BLOCKS);
-  d.ytarget = uint32_t(ep.G * (L->hidden / dl::RC));
+  d.step = reinterpret_cast<uint32_t*>(ws + o.ticket) + 1;  // the words after the route kernel's ticket
+  d.done = reinterpret_cast<uint32_t*>(ws + o.ticket) + 2;
   int rc = SC_ERR_UNSUPPORTED;
   auto go = [&]<int KGU, int KD>() {
     if (L->dtype == SC_BF16) rc = dl::run<KGU, KD, __nv_bfloat16>(d, s, stage);

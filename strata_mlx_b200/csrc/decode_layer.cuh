@@ -41,6 +41,7 @@ struct LayerDev {
   Plan* plan;
   void* h;
   int T, H, I, Is, E, K, hstride;
+  int rt_groups;  // route kernel: the window's tokens are split over this many groups of blocks
   int64_t rb_gu, rb_d, rb_sgu, rb_sd;
   int dn_stage, dn_stages;
   // expert parallel: this rank's experts [e0, e1) (its gate/up/down blocks hold only those, expert e at e - e0);
@@ -49,11 +50,13 @@ struct LayerDev {
   int e0, e1;
   void *ypairs, *sout;
   // expert parallel over peer memory (peers null: not in use): the ranks' exchange buffers (this rank's mappings),
-  // G ranks, this one `rank`, `tl` tokens a rank; the layer reads window X[par] and writes pair outputs Y[par];
-  // xtarget / ytarget: the counts that mark them complete
+  // G ranks, this one `rank`, `tl` tokens a rank; the layer reads window X[par] (complete when its count reaches
+  // xtarget) and writes pair outputs Y[par] as words tagged with the call's step number
   const uint64_t* peers;
   int G, rank, tl, par;
-  uint32_t xtarget, ytarget;
+  uint32_t xtarget;
+  uint32_t* step;  // the layer call's step number (this rank's workspace), counted up by the route kernel
+  uint32_t* done;  // the down kernel's blocks, counted up once each per call (this rank's workspace)
 };
 
 }  // namespace dl

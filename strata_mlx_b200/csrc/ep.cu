@@ -3,9 +3,9 @@
 // buffers into each other (layout and counters in ep.cuh).
 //
 //   ep_feed_kernel     a step's first window: this rank's tokens into every rank's X[0], then a count there
-//   ep_combine_kernel  once Y[p] counts full: moe_combine of this rank's tokens (strata_mlx/fused.py:467-481, the
-//                      fixed add order) into `out`, and, unless the layer is the chain's last, into every rank's
-//                      X[p ^ 1] with a count there
+//   ep_combine_kernel  moe_combine of this rank's tokens (strata_mlx/fused.py:467-481, the fixed add order) from
+//                      the words of Y[p] tagged with this call's step, into `out`, and, unless the layer is the
+//                      chain's last, into every rank's X[p ^ 1] with a count there
 // Every wait is bounded (ep::wait_count); a rank that never writes makes the others record SC_ERR_TIMEOUT and go on.
 #include <cuda.h>
 
@@ -36,10 +36,11 @@ __device__ unsigned long long g_eptrace[64][4];
 template <typename T>
 __global__ void __launch_bounds__(256) ep_feed_kernel(EpArgs A) {
   const size_t xo = xoff(0, A.T, A.H);
-  const int n = A.tl * A.H;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const T v = static_cast<const T*>(A.x)[i];
-    for (int g = 0; g < A.G; ++g) reinterpret_cast<T*>(A.peers[g] + xo)[int64_t(A.rank) * n + i] = v;
+  const int n = A.tl * A.H, n8 = n / 8;  // eight values (16 bytes) a store; hidden sizes are multiples of 256
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += gridDim.x * blockDim.x) {
+    const uint4 v = reinterpret_cast<const uint4*>(A.x)[i];
+    for (int g = 0; g < A.G; ++g)
+      reinterpret_cast<uint4*>(reinterpret_cast<T*>(A.peers[g] + xo) + int64_t(A.rank) * n)[i] = v;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -50,32 +51,64 @@ __global__ void __launch_bounds__(256) ep_feed_kernel(EpArgs A) {
 
 template <typename T>
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpArgs A) {
-  // Launched as a programmatic dependent of the down kernel, with no wait on it: the pair-output count says when
-  // every rank's down kernel (this rank's too, whose shared expert outputs this kernel reads) has written.
+  // Launched as a programmatic dependent of this rank's down kernel, with no wait on it: the words of Y carry the
+  // step of the call that wrote them (the pairs' ranks' down kernels), and this rank's down kernel counts its
+  // blocks once their shared expert outputs (local) are written; the routes were written before that.
   pdl_launch_dependents();  // the next layer's route kernel may load its weights now
   const uint64_t own = A.peers[A.rank];
   EP_TRACE(0);
+  // the window's count of this layer: its route and gate/up kernels are done with it (they ran before this rank's
+  // down kernel, which launched this one); no rank counts window p again before this rank's combine counted the
+  // next window, below
+  if (threadIdx.x == 0 && blockIdx.x == 0) *at_u32(own, xcount_off(A.par)) = 0;
+  __shared__ uint32_t s_step;
   if (threadIdx.x == 0) {
-    wait_count(at_u32(own, ycount_off(A.par)), A.ytarget, A.err);
-    // the window's count of this layer: its route and gate/up kernels are done (this rank's down kernel waited
-    // for them before it counted)
-    if (blockIdx.x == 0) *at_u32(own, xcount_off(A.par)) = 0;
+    // the step is final: the route kernel counted it before the down kernel, which launched this one, started
+    const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(A.step);
+    s_step = step;
+    // every down block of this call has written its rows (a monotonic count: dn_blocks a call)
+    wait_count(A.done, step * A.dn_blocks, A.err);
   }
   __syncthreads();
+  const uint32_t step = s_step;
   EP_TRACE(1);
-  const T* y = reinterpret_cast<const T*>(own + yoff(A.par, A.T, A.tl, A.K, A.H));
+  const uint64_t* y = reinterpret_cast<const uint64_t*>(own + yoff(A.par, A.T, A.tl, A.K, A.H));
   const size_t xo = xoff(A.par ^ 1, A.T, A.H);
-  const int n = A.tl * A.H;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int j = i / A.H, c = i % A.H, tok = A.rank * A.tl + j;
-    float yk[TOPK_MAX_K];
-    for (int k = 0; k < A.K; ++k) yk[k] = to_f32(y[(int64_t(j) * A.K + k) * A.H + c]);
+  const int n = A.tl * A.H, n4 = n / 4;
+  // four outputs a thread: every pair's two tagged words loaded at once, then checked (and waited for, rarely);
+  // groups of four dealt over the blocks in turn, so that every block has a share of a small window
+  for (int i = blockIdx.x + gridDim.x * threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    const int j = (4 * i) / A.H, c = (4 * i) % A.H, tok = A.rank * A.tl + j;
+    uint64_t w0[TOPK_MAX_K], w1[TOPK_MAX_K];
+#pragma unroll
+    for (int k = 0; k < TOPK_MAX_K; ++k)
+      if (k < A.K) load_words2(y + (int64_t(j) * A.K + k) * (A.H / 2) + c / 2, w0[k], w1[k]);
+    uint32_t yv[TOPK_MAX_K][2];
+#pragma unroll
+    for (int k = 0; k < TOPK_MAX_K; ++k)
+      if (k < A.K) {
+        const uint64_t* wk = y + (int64_t(j) * A.K + k) * (A.H / 2) + c / 2;
+        yv[k][0] = uint32_t(w0[k] >> 32) == step ? uint32_t(w0[k]) : wait_tagged(wk, step, A.err);
+        yv[k][1] = uint32_t(w1[k] >> 32) == step ? uint32_t(w1[k]) : wait_tagged(wk + 1, step, A.err);
+      }
+    uint2 sraw = make_uint2(0, 0);
+    if (A.Is > 0) sraw = *reinterpret_cast<const uint2*>(static_cast<const T*>(A.sout) + int64_t(tok) * A.H + c);
     const float gv = A.Is > 0 ? round_to<T>(A.gsh[tok]) : -INFINITY;
-    const float sv = A.Is > 0 ? to_f32(static_cast<const T*>(A.sout)[int64_t(tok) * A.H + c]) : 0.f;
-    const T v = from_f32<T>(combine_one<T>(yk, A.wts + tok * A.K, A.K, gv, sv));
-    static_cast<T*>(A.out)[i] = v;
+    uint2 ov;
+    T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float yk[TOPK_MAX_K];
+#pragma unroll
+      for (int k = 0; k < TOPK_MAX_K; ++k)
+        if (k < A.K) yk[k] = to_f32(reinterpret_cast<const T*>(&yv[k][q >> 1])[q & 1]);
+      const float sv = A.Is > 0 ? to_f32(reinterpret_cast<const T*>(&sraw)[q]) : 0.f;
+      o[q] = from_f32<T>(combine_one<T>(yk, A.wts + tok * A.K, A.K, gv, sv));
+    }
+    reinterpret_cast<uint2*>(A.out)[i] = ov;
     if (!A.last)
-      for (int g = 0; g < A.G; ++g) reinterpret_cast<T*>(A.peers[g] + xo)[int64_t(A.rank) * n + i] = v;
+      for (int g = 0; g < A.G; ++g)
+        reinterpret_cast<uint2*>(reinterpret_cast<T*>(A.peers[g] + xo) + int64_t(A.rank) * n)[i] = ov;
   }
   __syncthreads();
   if (!A.last && threadIdx.x == 0) {
@@ -181,6 +214,7 @@ extern "C" size_t sc_ep_exchange_bytes(const sc_moe_layer* layer, int ranks, int
 extern "C" int sc_ep_feed(const sc_moe_layer* layer, const sc_ep_exchange* ex, const void* x, void* stream) {
   if (int rc = check_ex(layer, ex)) return rc;
   if (!x) return SC_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) & 15) return SC_ERR_ALIGN;  // read 16 bytes at a time
   ep::EpArgs A{};
   A.peers = ex->peers;
   A.G = ex->ranks, A.rank = ex->rank, A.tl = ex->tokens_per_rank, A.T = ex->ranks * ex->tokens_per_rank;

@@ -186,6 +186,7 @@ extern "C" int sc_ep_combine(const sc_moe_layer* L, const sc_ep_exchange* ex, in
   if (!ex || !ex->peers || !ex->own || ex->ranks < 1 || ex->rank < 0 || ex->rank >= ex->ranks ||
       ex->tokens_per_rank < 1 || (parity != 0 && parity != 1) || !out)
     return SC_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(out) & 15) return SC_ERR_ALIGN;  // written 16 bytes at a time
   const int tokens = ex->ranks * ex->tokens_per_rank;
   if (int rc = check_layer(L, tokens)) return rc;
   const MoeWs m = moe_ws(L, tokens);
@@ -200,7 +201,9 @@ extern "C" int sc_ep_combine(const sc_moe_layer* L, const sc_ep_exchange* ex, in
   A.sout = ws + m.sout;
   A.out = out;
   A.err = reinterpret_cast<int*>(ws + m.err);
-  A.ytarget = uint32_t(ex->ranks * (L->hidden / dl::RC));
+  A.step = reinterpret_cast<const uint32_t*>(ws + m.ticket) + 1;  // the layer's decode kernels share these words
+  A.done = reinterpret_cast<const uint32_t*>(ws + m.ticket) + 2;
+  A.dn_blocks = uint32_t(L->hidden / dl::RC);
   return ep::combine_launch(A, L->dtype, static_cast<cudaStream_t>(stream));
 }
 
