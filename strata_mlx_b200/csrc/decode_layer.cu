@@ -745,8 +745,8 @@ int v2_run(const sc_moe_layer* L, const void* x, int tokens, void* out, uint8_t*
   d.tl = ep.tl;
   d.par = ep.par;
   d.xtarget = uint32_t(ep.G * ep::COMBINE_BLOCKS);
-  d.step = reinterpret_cast<uint32_t*>(ws + o.ticket) + 1;  // the words after the route kernel's ticket
-  d.done = reinterpret_cast<uint32_t*>(ws + o.ticket) + 2;
+  d.step = ep.step;
+  d.done = ep.done;
   int rc = SC_ERR_UNSUPPORTED;
   auto go = [&]<int KGU, int KD>() {
     if (L->dtype == SC_BF16) rc = dl::run<KGU, KD, __nv_bfloat16>(d, s, stage);

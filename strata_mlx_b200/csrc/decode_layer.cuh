@@ -55,8 +55,8 @@ struct LayerDev {
   const uint64_t* peers;
   int G, rank, tl, par;
   uint32_t xtarget;
-  uint32_t* step;  // the layer call's step number (this rank's workspace), counted up by the route kernel
-  uint32_t* done;  // the down kernel's blocks, counted up once each per call (this rank's workspace)
+  uint32_t* step;  // the layer call's step number (this rank's exchange buffer), counted up by the route kernel
+  uint32_t* done;  // the down kernel's blocks, counted up once each per call (this rank's exchange buffer)
 };
 
 }  // namespace dl
@@ -71,6 +71,8 @@ struct V2Ep {
   void* ypairs = nullptr;
   const uint64_t* peers = nullptr;  // peer-memory exchange (see ep.cuh); ypairs unused then
   int G = 1, rank = 0, tl = 0, par = 0;
+  uint32_t* step = nullptr;  // this rank's exchange buffer's step and down-block counts (ep.cuh)
+  uint32_t* done = nullptr;
 };
 
 // h rows of the down product are padded by 32 elements so that the tokens' rows fall on different banks

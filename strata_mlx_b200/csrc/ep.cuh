@@ -2,7 +2,10 @@
 // the release / acquire counters that mark a window complete, and the tagged words of the pair outputs.
 //
 // Layout of a rank's exchange buffer (the same on every rank):
-//   [0, 512)       counters: xcount[p] at 128 p (window p complete)
+//   [0, 512)       counters: xcount[p] at 128 p (window p complete); at 256 the step, this rank's count of layer
+//                  calls on this buffer (the route kernel adds one a call: every call's pair outputs get a tag of their
+//                  own, though the layers alternate two halves of Y; every rank counts alike); at 384 the down
+//                  kernel's blocks of every call, each once (a combine waits for step x blocks a call)
 //   X[p], p = 0, 1 the window of every rank's tokens, (T, H) of the activations' type, rank r's at rows r t ..
 //   Y[p], p = 0, 1 this rank's tokens' pair outputs, (t, K, H / 2) 64-bit words, written by the ranks that own the
 //                  pairs' experts: a word is two values of the activations' type (low half) and the layer call's
@@ -27,6 +30,7 @@ inline __host__ __device__ size_t yoff(int p, int T, int t, int K, int H) {
 }
 inline __host__ __device__ size_t total_bytes(int T, int t, int K, int H) { return yoff(2, T, t, K, H); }
 inline __host__ __device__ size_t xcount_off(int p) { return size_t(128) * p; }
+constexpr size_t STEP_OFF = 256, DONE_OFF = 384;
 
 __device__ __forceinline__ uint32_t* at_u32(uint64_t base, size_t off) {
   return reinterpret_cast<uint32_t*>(base + off);
@@ -96,8 +100,8 @@ struct EpArgs {
   const void* x;           // feed: this rank's tokens
   void* out;               // combine: this rank's tokens' outputs
   int* err;
-  const uint32_t* step;    // combine: the layer call's step number (this rank's workspace)
-  const uint32_t* done;    // combine: the down kernel's blocks count here (this rank's workspace), `dn_blocks` a call
+  const uint32_t* step;    // combine: the layer call's step number (this rank's exchange buffer, STEP_OFF)
+  const uint32_t* done;    // combine: the down kernel's blocks count here (DONE_OFF), `dn_blocks` a call
   uint32_t dn_blocks;
 };
 

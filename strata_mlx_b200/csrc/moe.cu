@@ -177,6 +177,8 @@ extern "C" int sc_moe_decode_layer_ep_p2p(const sc_moe_layer* L, const sc_ep_exc
   e.rank = ex->rank;
   e.tl = ex->tokens_per_rank;
   e.par = parity;
+  e.step = reinterpret_cast<uint32_t*>(ex->own + ep::STEP_OFF);
+  e.done = reinterpret_cast<uint32_t*>(ex->own + ep::DONE_OFF);
   return v2_run(L, window, tokens, nullptr, static_cast<uint8_t*>(workspace), o, static_cast<cudaStream_t>(stream), -1,
                 e);
 }
@@ -201,8 +203,8 @@ extern "C" int sc_ep_combine(const sc_moe_layer* L, const sc_ep_exchange* ex, in
   A.sout = ws + m.sout;
   A.out = out;
   A.err = reinterpret_cast<int*>(ws + m.err);
-  A.step = reinterpret_cast<const uint32_t*>(ws + m.ticket) + 1;  // the layer's decode kernels share these words
-  A.done = reinterpret_cast<const uint32_t*>(ws + m.ticket) + 2;
+  A.step = reinterpret_cast<const uint32_t*>(ex->own + ep::STEP_OFF);  // counts every layer call on the buffer
+  A.done = reinterpret_cast<const uint32_t*>(ex->own + ep::DONE_OFF);
   A.dn_blocks = uint32_t(L->hidden / dl::RC);
   return ep::combine_launch(A, L->dtype, static_cast<cudaStream_t>(stream));
 }

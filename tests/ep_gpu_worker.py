@@ -28,6 +28,9 @@ def main():
     dev = torch.device("cuda", local)
     bad = 0
     chain_one, chain_par = [], []
+    # more wrappers of the same layers (each with a workspace of its own): a chain of distinct layer objects whose
+    # calls reuse each half of the exchange buffer within one step
+    extra = []
     for kinds in (("IQ3_S", "IQ3_S", "Q2_0"), ("Q2_0", "Q2_0", "IQ3_XXS")):
         L = layer_numpy(np.random.default_rng(5), H, I, E, kinds, shared_inter=S)
         cu = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in L.items()
@@ -46,6 +49,8 @@ def main():
                                   shared_gate=cu["shared_gate"])
         chain_one.append(one)
         chain_par.append(par)
+        extra.append([EP.EPMoEDecodeLayer(cu["router"], mine["gate"], mine["up"], mine["down"], K, E, shared=shared,
+                                          shared_gate=cu["shared_gate"]) for _ in range(2)])
         for t in (1, 2):
             x = torch.randn((t, H), generator=torch.Generator(device=dev).manual_seed(10 * rank + t), device=dev)
             x = x.to(torch.bfloat16)
@@ -91,6 +96,26 @@ def main():
                 bad += 1
                 diff = (got.float() - want.float()).abs().max().item()
                 print(f"rank {rank} refed chain t={t} step {step}: differs (max {diff})", flush=True)
+        dist.barrier()
+        chain.close()
+    # six distinct layer objects fed again every two layers: window halves and pair-output halves are reused by
+    # other layers in the same step (their tags must still be this call's), the result the last two layers on x
+    for t in (1, 2):
+        chain = EP.EPDecodeChain([chain_par[0], chain_par[1], extra[0][0], extra[1][0], extra[0][1], extra[1][1]], t,
+                                 dev)
+        for step in range(3):
+            x = torch.randn((t, H), generator=torch.Generator(device=dev).manual_seed(2000 + 100 * step + 10 * rank + t),
+                            device=dev).to(torch.bfloat16)
+            got = chain(x, refeed=2).clone()
+            want = x
+            for one in chain_one:
+                want = torch.cat([one(want[i : i + 1]) for i in range(t)])
+            torch.cuda.synchronize()
+            chain.check_errors()
+            if not torch.equal(got, want):
+                bad += 1
+                diff = (got.float() - want.float()).abs().max().item()
+                print(f"rank {rank} six-layer chain t={t} step {step}: differs (max {diff})", flush=True)
         dist.barrier()
         chain.close()
     flag = torch.tensor([bad], device=dev)
