@@ -166,7 +166,9 @@ __host__ __device__ inline SmmaSmem smma_smem(int cols, int d_step, int tokens) 
   s.codes = o; o += SMMA_ROWS * s.cstride;
   s.scales = o; o += align16(SMMA_ROWS * (cols / 16));
   s.d = o; o += align16(SMMA_ROWS * (cols / d_step) * 2);
-  s.sfl = o; o += SMMA_ROWS * (cols / 16) * 4;  // scale * d of every row's groups, float32
+  // scale * d of every row's groups, float32, rows sfl_stride() apart: a stride of 4 words more than the groups, so
+  // that the eight rows a warp's lanes read at once fall on different banks (256 groups: all on one otherwise)
+  s.sfl = o; o += SMMA_ROWS * (cols / 16 + 4) * 4;
   s.xs = o; o += align16(tokens * cols * 2);
   s.red = o; o += SMMA_WARPS * 32 * 4 * 4;
   s.total = o;
@@ -182,47 +184,55 @@ __global__ void __launch_bounds__(SMMA_WARPS * 32) scaled_mma_kernel(const int8_
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const SmmaSmem S = smma_smem(cols, d_step, tokens);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bar);  // [w]: warp w's column slice; [SMMA_WARPS]: scales
+  // bars[0]: the block's rows of codes, one bulk copy a row (into rows padded by 16 bytes: the eight rows a warp's
+  // lanes read at once fall on different banks); bars[1]: their scales. One copy a row, not one a warp's column
+  // slice of a row: the copy engine's cost per copy, not the bytes, had set the kernel's pace.
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S.bar);
   const int r0 = blockIdx.x * SMMA_ROWS, nrow = min(SMMA_ROWS, rows - r0);
   const int groups = cols / 16, dper = cols / d_step, gper = d_step / 16;
   const int j0 = warp * groups / SMMA_WARPS, j1 = (warp + 1) * groups / SMMA_WARPS;
   if (tid == 0) {
-    for (int i = 0; i <= SMMA_WARPS; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (lane == 0) {  // each warp asks for its own slice of the rows (the copies go out from eight warps at once)
-    if (warp == 0) {
-      mbar_arrive_expect_tx(&bars[SMMA_WARPS], uint32_t(nrow * groups));
-      bulk_load(smem + S.scales, scales + int64_t(r0) * groups, uint32_t(nrow * groups), &bars[SMMA_WARPS]);
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[1], uint32_t(nrow * groups));
+      bulk_load(smem + S.scales, scales + int64_t(r0) * groups, uint32_t(nrow * groups), &bars[1]);
+      mbar_arrive_expect_tx(&bars[0], uint32_t(nrow) * uint32_t(cols));
     }
-    const uint32_t slice = uint32_t(16 * (j1 - j0));
-    mbar_arrive_expect_tx(&bars[warp], uint32_t(nrow) * slice);
-    for (int rr = 0; rr < nrow; ++rr)
-      bulk_load(smem + S.codes + rr * S.cstride + 16 * j0, codes + int64_t(r0 + rr) * cols + 16 * j0, slice,
-                &bars[warp]);
+    __syncwarp();
+    if (lane < nrow)
+      bulk_load(smem + S.codes + lane * S.cstride, codes + int64_t(r0 + lane) * cols, uint32_t(cols), &bars[0]);
   }
+  // the next kernel of the stream (the next layer, launched the same way) may fetch its weights from now on; it
+  // reads this one's output only after its own wait below
+  pdl_launch_dependents();
   __half* dsm = reinterpret_cast<__half*>(smem + S.d);
   for (int i = tid; i < nrow * dper; i += blockDim.x) dsm[i] = d[int64_t(r0) * dper + i];
-  T* xs = reinterpret_cast<T*>(smem + S.xs);
-  for (int i = tid; i < tokens * cols / 8; i += blockDim.x)
-    reinterpret_cast<uint4*>(xs)[i] = __ldg(reinterpret_cast<const uint4*>(x) + i);
   __syncthreads();
-  bool ok = mbar_wait_sleep(&bars[SMMA_WARPS], 0, err);
+  bool ok = mbar_wait_sleep(&bars[1], 0, err);
   float* sfl = reinterpret_cast<float*>(smem + S.sfl);
   const int8_t* ssm = reinterpret_cast<const int8_t*>(smem + S.scales);
   const int gshift = __ffs(gper) - 1;  // d_step / 16, a power of two
+  const int fstride = groups + 4;
   for (int rr = 0; rr < nrow; ++rr)
     for (int j = tid; j < groups; j += blockDim.x)
-      sfl[rr * groups + j] = __half2float(dsm[rr * dper + (j >> gshift)]) * float(ssm[rr * groups + j]);
+      sfl[rr * fstride + j] = __half2float(dsm[rr * dper + (j >> gshift)]) * float(ssm[rr * groups + j]);
+  pdl_wait();  // the activations: the previous kernel's output
+  T* xs = reinterpret_cast<T*>(smem + S.xs);
+  for (int i = tid; i < tokens * cols / 8; i += blockDim.x)
+    reinterpret_cast<uint4*>(xs)[i] = __ldcg(reinterpret_cast<const uint4*>(x) + i);
   __syncthreads();
-  ok = ok && mbar_wait_sleep(&bars[warp], 0, err);
+  ok = ok && mbar_wait_sleep(&bars[0], 0, err);
 
   const int g = lane >> 2, t = lane & 3;
   const uint8_t* ca = smem + S.codes + g * S.cstride + 4 * t;
   const uint8_t* cb = ca + 8 * S.cstride;
-  const float* sa = sfl + g * groups;
-  const float* sb = sa + 8 * groups;  // rows past nrow: stale values, in rows never written out
+  const float* sa = sfl + g * fstride;
+  const float* sb = sa + 8 * fstride;  // rows past nrow: stale values, in rows never written out
   const bool mine = g < tokens;
   const T* xg = xs + g * cols + 4 * t;
   constexpr uint32_t HI = Bias<T>::hi * 0x01010101u, SUB = Bias<T>::pair + 0x00200020u;  // bias + 32: code + 32 - it
@@ -301,10 +311,22 @@ extern "C" int sc_scaled_matvec(const void* codes, const void* scales, const voi
         if constexpr (sizeof(T) == 2) {
           auto kern = scaled_mma_kernel<T>;
           e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-          if (e == cudaSuccess)
-            kern<<<int(ceil_div(rows, SMMA_ROWS)), SMMA_WARPS * 32, smem, static_cast<cudaStream_t>(stream)>>>(
-                static_cast<const int8_t*>(codes), static_cast<const int8_t*>(scales), static_cast<const __half*>(d),
-                rows, cols, d_step, static_cast<const T*>(x), tokens, static_cast<T*>(out), err);
+          if (e == cudaSuccess) {
+            // programmatic dependent launch: the weights' copies go out while the kernel before finishes
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(unsigned(ceil_div(rows, SMMA_ROWS)));
+            cfg.blockDim = dim3(SMMA_WARPS * 32);
+            cfg.dynamicSmemBytes = size_t(smem);
+            cfg.stream = static_cast<cudaStream_t>(stream);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, kern, static_cast<const int8_t*>(codes), static_cast<const int8_t*>(scales),
+                                   static_cast<const __half*>(d), rows, cols, d_step, static_cast<const T*>(x),
+                                   tokens, static_cast<T*>(out), err);
+          }
         }
       });
       if (e != cudaSuccess) return SC_ERR_CUDA;
