@@ -809,6 +809,76 @@ def config5_result(world: int, rank: int, device, group=None, steps: int = 256, 
     return res
 
 
+def paged_result(steps: int = 200, warmup: int = 20, budget_experts: int = 128) -> dict:
+    """The paged expert store (strata_mlx_b200/paged.py, strata_mlx/paged.py:105-419): one configuration-2 layer
+    of IQ3_S experts (512 x gate/up 2048 -> 512, down 512 -> 2048) written to a GGUF file, served by
+    PagedSwitchGLU within a budget of `budget_experts` experts, one token a call with seeded uniform top-10 routes:
+    each call waits for its routes on the host, reads the experts the store lacks (the file is in the page cache,
+    having just been written) and runs the separate-expert kernels. Beside it, the same layer resident
+    (BlockSwitchGLU)."""
+    import tempfile
+
+    import gguf
+    from gguf import GGMLQuantizationType as Q
+
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import gguf as G
+    from strata_mlx_b200 import paged as P
+    from strata_mlx_b200.synthetic import blocks_numpy
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(21)
+    kind = "IQ3_S"
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "layer.gguf")
+        w = gguf.GGUFWriter(path, "bench")
+        for name, (rows, cols) in (("up", (I, H)), ("gate", (I, H)), ("down", (H, I))):
+            a = blocks_numpy(kind, E, rows, cols, rng, sigma=EP_SIGMA[kind]).reshape(E, rows, -1)
+            w.add_tensor(f"blk.0.ffn_{name}_exps.weight", a, raw_dtype=Q.IQ3_S)
+        w.write_header_to_file()
+        w.write_kv_data_to_file()
+        w.write_tensors_to_file()
+        w.close()
+        f = G.GGUF(path)
+        gate, up, down = (f[f"blk.0.ffn_{n}_exps.weight"] for n in ("gate", "up", "down"))
+        size = sum(t.data.nbytes // t.shape[0] for t in (gate, up, down))
+        store = P.ExpertStore(budget_experts * size, device=device)
+        layer = P.PagedSwitchGLU(0, store, gate, up, down)
+        resident = B.BlockSwitchGLU(*(B.BlockSwitchLinear(G.to_device(t, device), t.type, t.shape)
+                                      for t in (gate, up, down)))
+        xs = torch.randn((steps + warmup, 1, H), device=device).to(torch.bfloat16)
+        idx = torch.from_numpy(np.stack([rng.choice(E, K, replace=False) for _ in range(steps + warmup)])
+                               .astype(np.int32)).to(device).reshape(steps + warmup, 1, K)
+
+        def run(fn, first, n):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for i in range(first, first + n):
+                fn(xs[i], idx[i])
+            torch.cuda.synchronize()
+            return (time.perf_counter() - t0) / n
+
+        run(layer, 0, warmup)
+        store.reset_stats()
+        paged_s = run(layer, warmup, steps)
+        stats = {"hits": store.hits, "misses": store.misses, "bytes_read": store.bytes_read, "read_s": store.read_s}
+        run(resident, 0, warmup)
+        resident_s = run(resident, warmup, steps)
+        del store, layer, resident, f
+    torch.cuda.empty_cache()
+    return {"api": "strata_mlx_b200.paged.PagedSwitchGLU.__call__ (ExpertStore, budget of "
+                   f"{budget_experts} of {E} experts)",
+            "workload": "one configuration-2 layer of IQ3_S experts from a GGUF file, one token a call, uniform "
+                        "random top-10 routes; the file in the page cache",
+            "calls": steps, "ms_per_call": paged_s * 1e3, "calls_per_s": 1.0 / paged_s,
+            "hit_rate": stats["hits"] / max(1, stats["hits"] + stats["misses"]),
+            "read_bytes_per_call": stats["bytes_read"] / steps,
+            "read_gbs": stats["bytes_read"] / max(stats["read_s"], 1e-9) / 1e9,
+            "resident_ms_per_call": resident_s * 1e3,
+            "note": "each call waits on the host for its routes (as the reference does); reads are file -> pinned "
+                    "host memory -> device"}
+
+
 def stage_bytes(kind: str) -> dict:
     """Algorithmic bytes of each of the three kernels of one layer, one token: every byte a kernel must read or
     write once (routed experts: 10 distinct, one token)."""
@@ -1218,6 +1288,7 @@ def main() -> None:
         torch.cuda.synchronize()
         line["config1"] = config1_result(cpu_seconds=None if args.no_cpu_baseline else 5.0)
         line["mid_batch"] = mid_batch_result()
+        line["paged"] = paged_result()
         line["prefill"] = prefill_result(20, 5, None if args.no_cpu_baseline else 6.0)
         line["config4"] = config4_result(world, rank, device)
         line["config5"] = config5_result(world, rank, device, steps=args.config5_steps)
