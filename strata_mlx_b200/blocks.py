@@ -111,9 +111,13 @@ class BlockSwitchLinear:
             share = k
         else:
             x, share = torch.broadcast_to(x, (*indices.shape, 1, self.input_dims)), 1
-        pairs = indices.numel()
-        if pairs >= self.unpack_from:
+        if indices.numel() >= self.unpack_from:
             return self._as_floats(x, indices, share)
+        return self._pairs(x, indices, share)
+
+    def _pairs(self, x: torch.Tensor, indices: torch.Tensor, share: int) -> torch.Tensor:
+        """Each pair's product straight from the blocks (sc_expert_matvec)."""
+        pairs = indices.numel()
         idx = _contig(indices.reshape(-1).to(torch.int32)).view(torch.uint32)
         xs = _contig(x.reshape(-1, self.input_dims))
         out = torch.empty((pairs, self.output_dims), dtype=x.dtype, device=x.device)
@@ -126,8 +130,8 @@ class BlockSwitchLinear:
     def _as_floats(self, x: torch.Tensor, indices: torch.Tensor, share: int) -> torch.Tensor:
         """Many pairs at once (the reference unpacks the stack for MLX's gather_mm, blocks.py:438-440). For a stack
         the tile products take, the pairs go through tiles_of and tile_matmul on the GPU, weights rounded to the
-        activations' type as gather_mm's are: no host synchronization. Other shapes: the stack dequantized and a
-        product per expert."""
+        activations' type as gather_mm's are: no host synchronization. Other shapes and float32 activations stay on
+        the pair-at-a-time kernel, the weights exact: no float copy of the stack, no host synchronization."""
         if x.dtype in (torch.float16, torch.bfloat16) and tileable(self.kind, self.output_dims, self.input_dims):
             flat = indices.reshape(-1, 1)
             tiles, token, where = tiles_of(flat, self.num_experts)
@@ -136,15 +140,7 @@ class BlockSwitchLinear:
             c = tile_matmul(self.blocks, self.kind, (self.num_experts, self.output_dims, self.input_dims), a, tiles)
             out = c.index_select(0, where.to(torch.int64)).to(x.dtype)
             return out.reshape(*indices.shape, 1, self.output_dims)
-        w = dequantize(self.blocks, self.kind, (self.num_experts, self.output_dims, self.input_dims), x.dtype)
-        flat = indices.reshape(-1).long()
-        xs = x.reshape(-1, self.input_dims)
-        rows = torch.arange(flat.numel(), device=x.device) // share
-        out = torch.empty((flat.numel(), self.output_dims), dtype=x.dtype, device=x.device)
-        for e in torch.unique(flat).tolist():
-            sel = (flat == e).nonzero().squeeze(1)
-            out[sel] = (xs[rows[sel]].float() @ w[e].float().T).to(x.dtype)
-        return out.reshape(*indices.shape, 1, self.output_dims)
+        return self._pairs(x, indices, share)
 
 
 def matvec_separate(experts: list, kind: str, rows: int, cols: int, x: torch.Tensor, share: int) -> torch.Tensor:
