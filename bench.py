@@ -1146,10 +1146,11 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--kinds", default="mixed", choices=["mixed", "Q2_0", "IQ3_S"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "chain", "mid"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "chain", "mid", "dense"],
                     help="decode: configuration 2, the headline line; prefill: configuration 3 (one GPU); chain: the "
                          "persistent chain kernel alone (one GPU, for profiling); mid: the mid_batch sub-line alone "
-                         "(--steps replays, min(--layers, 3) layers a block type)")
+                         "(--steps replays, min(--layers, 3) layers a block type); dense: the Q6_K dense_stream "
+                         "sub-line alone (--layers layers, --steps replays)")
     ap.add_argument("--tokens", type=int, default=1, help="--workload chain: the window's tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config5-steps", type=int, default=256, help="greedy decode steps of the configuration-5 line")
@@ -1169,6 +1170,15 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
+    if args.workload == "dense":  # one GPU: the Q6_K layers alone, for timing and profiling them
+        from strata_mlx_b200 import _lib
+
+        _lib.load()
+        device = torch.device("cuda", torch.cuda.current_device())
+        ds = dense_stream(device, n_layers=args.layers, reps=args.steps)
+        ds["frac"] = ds["gbs"] / peaks()["hbm_gbs"]
+        print(json.dumps({"workload": "dense", **ds}), flush=True)
+        return
     if args.workload == "mid":
         if rank == 0:
             from strata_mlx_b200 import _lib
