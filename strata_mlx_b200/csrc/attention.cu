@@ -8,7 +8,8 @@
 //                       the 8 query heads of its group times the window as up to 64 rows,
 //                       streams the chunk's pages through shared memory (cp.async, three stages), and keeps an online
 //                       softmax: scores and the value product on mma.sync (bf16, f32 sums), probabilities rounded
-//                       to bf16 for the value product. A second kernel merges the chunks' partial results.
+//                       to bf16 for the value product. A second kernel, launched as its programmatic dependent,
+//                       merges the chunks' partial results.
 //
 // Query token i sits at position ctx_len - T_q + i and sees keys 0 .. its position (the window's own keys included:
 // they are in the cache before the call).
@@ -72,6 +73,7 @@ __global__ void __launch_bounds__(WARPS * 32) attn_kernel(const Args A) {
   const int ctx = *A.ctx_dev;
   const int k0 = chunk * A.cpages * PAGE, k1 = min(ctx, k0 + A.cpages * PAGE);
   const int pages = k1 > k0 ? (k1 - k0 + PAGE - 1) / PAGE : 0;
+  pdl_launch_dependents();  // the merge's blocks may be placed as this grid's blocks leave
   // Q rows: row r = token (r / GQA), query head hk * GQA + r % GQA
   for (int i = tid; i < MAXROWS * (D / 8); i += blockDim.x) {
     const int r = i / (D / 8), c = (i % (D / 8)) * 8;
@@ -197,13 +199,17 @@ __global__ void __launch_bounds__(WARPS * 32) attn_kernel(const Args A) {
   }
 }
 
-// out[token, head, d] = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c over the chunks c: a block per (row, head),
-// four groups of 256 threads (a dimension each) taking every fourth chunk, so that many loads are in flight
-constexpr int MERGE_GROUPS = 4;
+// out[token, head, d] = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c over the chunks c: a block per (row, head,
+// 32 dimensions), eight groups of 32 threads (a dimension each) taking every eighth chunk, so that the grid covers
+// many SMs and many loads are in flight. It waits for the attention kernel's partial results before reading them.
+constexpr int MERGE_DIMS = 32;
+constexpr int MERGE_GROUPS = 8;
 
-__global__ void __launch_bounds__(MERGE_GROUPS * D) merge_kernel(const Args A) {
-  __shared__ float s_w[1024], s_num[MERGE_GROUPS][D], s_den[MERGE_GROUPS];
-  const int row = blockIdx.x, hk = blockIdx.y, d = threadIdx.x % D, grp = threadIdx.x / D;
+__global__ void __launch_bounds__(MERGE_GROUPS * MERGE_DIMS) merge_kernel(const Args A) {
+  __shared__ float s_w[1024], s_num[MERGE_GROUPS][MERGE_DIMS], s_den[MERGE_GROUPS];
+  const int row = blockIdx.x, hk = blockIdx.y, grp = threadIdx.x / MERGE_DIMS;
+  const int d = blockIdx.z * MERGE_DIMS + threadIdx.x % MERGE_DIMS;
+  pdl_wait();
   const int rows = GQA * A.Tq;
   if (row >= rows) return;
   const int ctx = *A.ctx_dev;
@@ -222,14 +228,14 @@ __global__ void __launch_bounds__(MERGE_GROUPS * D) merge_kernel(const Args A) {
     num += s_w[c] * A.opart[b * D + d];
     den += s_w[c] * A.lpart[b];
   }
-  s_num[grp][d] = num;
-  if (d == 0) s_den[grp] = den;
+  s_num[grp][threadIdx.x % MERGE_DIMS] = num;
+  if (threadIdx.x % MERGE_DIMS == 0) s_den[grp] = den;
   __syncthreads();
   if (grp == 0) {
     float n = 0.f, dd = 0.f;
 #pragma unroll
     for (int g = 0; g < MERGE_GROUPS; ++g) {
-      n += s_num[g][d];
+      n += s_num[g][threadIdx.x % MERGE_DIMS];
       dd += s_den[g];
     }
     A.out[(int64_t(row / GQA) * A.Hq + hk * GQA + row % GQA) * D + d] = __float2bfloat16_rn(dd > 0.f ? n / dd : 0.f);
@@ -290,7 +296,19 @@ extern "C" int sc_paged_attention(const void* q, const void* k_cache, const void
   if (int rc = raise_smem(reinterpret_cast<const void*>(at::attn_kernel), smem, "attention smem attribute")) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   at::attn_kernel<<<dim3(A.chunks, kv_heads), at::WARPS * 32, smem, s>>>(A);
-  at::merge_kernel<<<dim3(at::GQA * tokens, kv_heads), at::MERGE_GROUPS * at::D, 0, s>>>(A);
+  {  // programmatic dependent launch: no gap between the two kernels
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(at::GQA * tokens), unsigned(kv_heads), unsigned(at::D / at::MERGE_DIMS));
+    cfg.blockDim = dim3(at::MERGE_GROUPS * at::MERGE_DIMS);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaError_t e = cudaLaunchKernelEx(&cfg, at::merge_kernel, A))
+      return cuda_failed(e, "attention merge launch");
+  }
   if (cudaError_t e = cudaGetLastError()) return cuda_failed(e, "attention launch");
   return SC_OK;
 }

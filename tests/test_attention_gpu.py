@@ -1,6 +1,7 @@
 """The paged grouped-query attention kernel (sc_paged_attention) of the synthetic decoder against a float32 torch
-reference of the same softmax(q k^T / 16) v on the same bfloat16 inputs: windows of 1, 5 and 8 new tokens, contexts
-that end inside a chunk and a page, the sequence's pages scattered through the cache."""
+reference of the same softmax(q k^T / 16) v on the same bfloat16 inputs: windows of 1 to 5 and 8 new tokens (the
+kernel's four-, two- and one-group forms), contexts that end inside a chunk, a page and a round of a group's pages,
+the sequence's pages scattered through the cache."""
 
 import math
 
@@ -26,8 +27,8 @@ def reference(q, kseq, vseq, ctx):
     return out
 
 
-@pytest.mark.parametrize("tokens", [1, 5, 8])
-@pytest.mark.parametrize("ctx", [5, 300, 1000, 4113])
+@pytest.mark.parametrize("tokens", [1, 2, 3, 4, 5, 8])
+@pytest.mark.parametrize("ctx", [5, 300, 1000, 4113, 20000])
 def test_paged_attention_is_the_softmax_product(cuda, tokens, ctx):
     if ctx < tokens:
         pytest.skip("the window is part of the context")
