@@ -123,3 +123,33 @@ def test_the_decode_block_refuses_pointers_off_16_bytes_before_any_launch():
     L = _decode_layer(base, {})
     n = lib.sc_moe_decode_workspace(ctypes.addressof(L), 1)
     assert lib.sc_moe_decode_stage(ctypes.addressof(L), x + 4, 1, x, ws, n, 1, None) == -4  # the window
+
+
+def test_paged_attention_workspace_and_refusals():
+    """sc_paged_attention's workspace holds, per chunk of whole 16-token pages (about 296 chunks over the key/value
+    heads), 64 rows of partial outputs (256 floats) with their maxima and sums, and 256 spare bytes; its argument
+    checks answer before any launch."""
+    lib = _lib.load()
+    for ctx, kv in ((1, 2), (300, 2), (8192, 2), (131072 + 272, 2), (20000, 1), (65536, 4)):
+        pages = -(-ctx // 16)
+        want = -(-296 // kv)
+        cpages = -(-pages // want)
+        chunks = -(-pages // cpages)
+        assert chunks <= want
+        assert lib.sc_paged_attention_workspace(ctx, kv) == chunks * kv * 64 * (256 * 4 + 8) + 256
+    assert lib.sc_paged_attention_workspace(0, 2) == 0 and lib.sc_paged_attention_workspace(8, 0) == 0
+    fake = 0x1000  # never dereferenced
+    ws = lib.sc_paged_attention_workspace(4096, 2)
+    f = ctypes.c_float(1 / 16)
+
+    def call(q=fake, ctx=4096, tokens=1, q_heads=16, kv_heads=2, head_dim=256, ws_bytes=ws, k=fake, table=fake):
+        return lib.sc_paged_attention(q, k, fake, table, fake, ctx, tokens, q_heads, kv_heads, head_dim, f, fake,
+                                      fake, ws_bytes, None)
+
+    assert call(table=None) == -5
+    assert call(head_dim=128) == -2
+    assert call(q_heads=12) == -2  # eight query heads a key/value head
+    assert call(tokens=0) == -2 and call(tokens=9) == -2
+    assert call(ctx=3, tokens=4) == -2  # the window is part of the context
+    assert call(q=fake + 8) == -4 and call(k=fake + 2) == -4
+    assert call(ws_bytes=ws - 1) == -7
