@@ -1,10 +1,13 @@
-"""The paged expert store's rules on the host (strata_mlx_b200/paged.py, the reference's strata_mlx/paged.py:105-370):
+"""The paged expert store's rules on the host (strata_mlx_b200/paged.py, the reference's strata_mlx/paged.py:105-419):
 the bytes it holds are the file's, the least recently used go first within the budget, a call keeps its own experts,
-a layer whole and a layer read ahead, preloading by counts and the counts it keeps. No GPU: the store on the CPU."""
+a layer whole and a layer read ahead, preloading by counts and the counts it keeps, and the layer's three ways to its
+products. No GPU: the store on the CPU, the kernels stood in for by the oracle."""
 
 import numpy as np
 import pytest
+import torch
 
+from oracle import blocks_ref as R
 from strata_mlx_b200 import paged as P
 
 from .paged_model import E, layer_tensors, write
@@ -89,7 +92,7 @@ def test_a_layer_read_ahead_is_what_its_hold_takes(model):
     s.get(1, ts, [5])
     s.ahead(1)
     s.hold(1)
-    stacks = s.kept[1]
+    stacks = s.kept.stacks
     for t, a in zip(ts, stacks):
         assert np.array_equal(a.numpy(), t.data.reshape(-1))
     got = s.get(1, ts, [0, 11], keep=False)  # slices of the held layer
@@ -118,3 +121,71 @@ def test_profiles_are_saved_and_loaded(tmp_path):
     P.save_profile(path, counts)
     assert np.array_equal(P.load_profile(path), counts)
     assert P.load_profile(str(tmp_path / "none.npy")) is None
+
+
+def test_reads_of_consecutive_experts_are_runs(model, monkeypatch):
+    s = store_for(model, 100)
+    ts = tensors(model)
+    calls = []
+    real = s._pread
+    monkeypatch.setattr(s, "_pread", lambda t, first, count: calls.append((first, count)) or real(t, first, count))
+    got = s.get(0, ts, [6, 2, 3, 4, 9])
+    assert sorted(set(calls)) == [(2, 3), (6, 1), (9, 1)] and len(calls) == 3 * len(ts)
+    for e, arrays in zip([6, 2, 3, 4, 9], got):
+        for t, a in zip(ts, arrays):
+            assert np.array_equal(a.numpy(), file_bytes(t, e))
+    assert s.bytes_read == 5 * expert_size(ts)
+
+
+class _Weights:
+    """Stands in for BlockSwitchLinear: the stack's weights through the oracle's decoder."""
+
+    def __init__(self, blocks, kind, shape):
+        self.w = R.dequantize(blocks.numpy(), kind, tuple(shape)).astype(np.float64)
+        self.unpack_from = 0
+
+
+def _silu_glu(g, u):
+    return g / (1.0 + np.exp(-g)) * u
+
+
+def _fake_switch_glu(x, indices, up, gate, down):
+    idx = indices.numpy().reshape(x.shape[0], -1)
+    xs = x.numpy()
+    out = np.zeros((*idx.shape, down.w.shape[1]))
+    for t in range(idx.shape[0]):
+        for j, e in enumerate(idx[t]):
+            out[t, j] = down.w[e] @ _silu_glu(gate.w[e] @ xs[t], up.w[e] @ xs[t])
+    return torch.from_numpy(out)
+
+
+def _fake_matvec_separate(experts, kind, rows, cols, x, share):
+    xs = x.numpy().reshape(-1, cols)
+    return torch.from_numpy(np.stack([R.dequantize(b.numpy(), kind, (1, rows, cols))[0].astype(np.float64)
+                                      @ xs[p // share] for p, b in enumerate(experts)]))
+
+
+def test_the_layer_takes_pairs_stacks_and_whole_layers_to_the_same_products(model, monkeypatch):
+    """PagedSwitchGLU on the host: a few pairs (each expert where it lies), a larger window (a stack of the experts it
+    uses, routes renumbered into it) and a prompt using most experts (the layer whole) give the products of the
+    file's own experts."""
+    monkeypatch.setattr(P, "BlockSwitchLinear", _Weights)
+    monkeypatch.setattr(P, "switch_glu", _fake_switch_glu)
+    monkeypatch.setattr(P, "matvec_separate", _fake_matvec_separate)
+    monkeypatch.setattr(P, "swiglu", lambda g, u: torch.from_numpy(_silu_glu(g.numpy(), u.numpy())))
+    gate, up, down = layer_tensors(model, 1)
+    wg, wu, wd = (R.dequantize(t.data, t.type, t.shape).astype(np.float64) for t in (gate, up, down))
+    s = P.ExpertStore(100 * expert_size((up, gate, down)), threads=4, device="cpu")
+    glu = P.PagedSwitchGLU(1, s, gate, up, down)
+    rng = np.random.default_rng(8)
+    width = up.shape[2]
+    for tokens, whole_from in ((5, P.WHOLE_FROM), (40, P.WHOLE_FROM), (40, 6)):
+        monkeypatch.setattr(P, "WHOLE_FROM", whole_from)
+        idx = np.stack([rng.choice(E, 4, replace=False) for _ in range(tokens)]).astype(np.int32)
+        idx[:, 0] = np.arange(tokens) % 7  # at most 10 distinct experts a window before the last case
+        x = rng.standard_normal((tokens, width)) * 0.1
+        got = glu(torch.from_numpy(x), torch.from_numpy(idx)).numpy()
+        want = np.stack([[wd[e] @ _silu_glu(wg[e] @ x[t], wu[e] @ x[t]) for e in idx[t]] for t in range(tokens)])
+        assert got.shape == (tokens, 4, width)
+        np.testing.assert_allclose(got, want, rtol=1e-9, atol=1e-12)
+    assert s.misses > 0 and s.hits > 0 and s.lru
