@@ -7,7 +7,6 @@ source in Python strings, so there is no oracle/_ref build.
 
 import os
 import subprocess
-import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "liboracle.so")

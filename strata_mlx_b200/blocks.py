@@ -21,7 +21,6 @@ reference's names so that tests can monkeypatch them as the reference's tests do
 
 from __future__ import annotations
 
-import ctypes
 
 import torch
 

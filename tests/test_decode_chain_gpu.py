@@ -11,7 +11,7 @@ import torch
 from oracle import blocks_ref as R
 from strata_mlx_b200 import blocks as B
 from strata_mlx_b200 import fused as F
-from strata_mlx_b200.synthetic import blocks_numpy, layer_numpy
+from strata_mlx_b200.synthetic import blocks_numpy
 from tests import decode_bar
 
 pytestmark = pytest.mark.gpu

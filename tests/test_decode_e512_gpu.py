@@ -9,7 +9,6 @@ import pytest
 import torch
 
 from oracle import blocks_ref as R
-from strata_mlx_b200 import _lib
 from strata_mlx_b200 import blocks as B
 from strata_mlx_b200 import fused as F
 from strata_mlx_b200.synthetic import layer_numpy
